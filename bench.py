@@ -1,0 +1,523 @@
+#!/usr/bin/env python
+"""Benchmark of the depthwise causal conv1d hot path on B200.
+
+python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-paths]
+
+Headline (the configuration the metric is quoted on): prefill of
+x (batch 8, seqlen 4096, dim 8192) bf16 ~N(0,1) stored token-major and passed as its
+(batch, dim, seqlen) view, weight (8192, 4) ~U(-0.5, 0.5), bias ~N(0, 0.1), SiLU. One step is one
+causal_conv1d_fn call over that batch. value = algorithmic bytes (every input element read once,
+every output element written once, plus weights and bias) / device time, summed over ranks.
+Inputs (512 MiB) exceed L2 (126 MB), so no flush is needed between steps.
+
+At N > 1 (torchrun, one rank per GPU) the layer is channel-sliced as tensor parallelism shards it:
+rank r owns channels [8192 r, 8192 (r + 1)) of a layer with 8192 N channels, so per-GPU work is
+fixed (weak scaling) and the kernels exchange nothing. NCCL is used once, after timing, to
+all-gather a sample of every rank's outputs and compare them bit for bit with the unsharded run.
+
+With N = 1 the other BASELINE paths are measured too ("paths"): indexed decode (config 3) and its
+ring variant, the 4-step speculative verify with dense per-step states (config 4), and packed
+varlen prefill (config 5) at widths 2, 3, 4 and 8. Decode inputs fit in L2, so every timed decode
+call is preceded by a write of 256 MiB (cold L2), and the warm figure is reported beside it.
+
+--impl reference times the reference's CPU algorithm (the C port of its PyTorch fallback,
+oracle/cc1d_oracle.c) on the host cores, on bounded samples of the same workload.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (str(ROOT / "causal-conv1d-cute_b200"), str(ROOT)):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "prefill/varlen achieved HBM GB/s vs ~8 TB/s; decode µs/call at bs=256"
+B, L, D, W = 8, 4096, 8192, 4
+E = 2  # bf16
+HEADLINE_BYTES = 2 * B * L * D * E + D * W * E + D * E  # 1,073,823,744
+L2_BYTES = 126 * 2**20
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--no-paths", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------
+# Peaks, clocks, profiles
+# ---------------------------------------------------------------------------------------------
+
+
+def peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(kernel):
+    """dram bytes per launch of `kernel` recorded in profiles/*.md ("traffic_bytes_per_launch")."""
+    for f in sorted((ROOT / "profiles").glob("*.md")):
+        kname = None
+        for line in f.read_text().splitlines():
+            if line.startswith("kernel:"):
+                kname = line.split(":", 1)[1].strip()
+            if line.startswith("traffic_bytes_per_launch:") and kname == kernel:
+                return int(float(line.split(":", 1)[1].strip()))
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML on a background thread."""
+
+    REASONS = {
+        "hw_slowdown": 0x8,
+        "hw_thermal_slowdown": 0x40,
+        "sw_thermal_slowdown": 0x20,
+        "sw_power_cap": 0x4,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index, period=0.01):
+        self.samples = []
+        self.period = period
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            handle = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                h = pynvml.nvmlDeviceGetHandleByIndex(i)
+                u = pynvml.nvmlDeviceGetUUID(h)
+                u = u.decode() if isinstance(u, bytes) else u
+                if u.replace("GPU-", "") == uuid.replace("GPU-", ""):
+                    handle = h
+            if handle is None:
+                handle = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.nvml, self.handle = pynvml, handle
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(handle, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.error = str(e)
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                util = n.nvmlDeviceGetUtilizationRates(self.handle).gpu
+                self.samples.append((mhz, reasons, util))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self.ok:
+            self._t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.error}
+        busy = [s for s in self.samples if s[2] > 0] or self.samples
+        mhz = [s[0] for s in busy]
+        seen = set()
+        for s in busy:
+            for name, bit in self.REASONS.items():
+                if s[1] & bit:
+                    seen.add(name)
+        return {
+            "sm_mhz": statistics.median(mhz) if mhz else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(seen),
+            "samples": len(busy),
+        }
+
+
+# ---------------------------------------------------------------------------------------------
+# Timing helpers
+# ---------------------------------------------------------------------------------------------
+
+
+def time_launches(step, steps, flush=None):
+    """Run `step` `steps` times on the current stream; return (total ms, per-launch ms list).
+
+    Each launch is bracketed by its own CUDA events (so a cold-L2 flush issued between launches is
+    not counted); the total spans the first start to the last end.
+    """
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        if flush is not None:
+            flush()
+        starts[i].record()
+        step()
+        ends[i].record()
+    torch.cuda.synchronize()
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    return starts[0].elapsed_time(ends[-1]), per
+
+
+_flush_buf = None
+
+
+def flush_l2():
+    global _flush_buf
+    if _flush_buf is None:
+        _flush_buf = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
+    _flush_buf.fill_(1)
+
+
+# ---------------------------------------------------------------------------------------------
+# Headline: prefill config 2
+# ---------------------------------------------------------------------------------------------
+
+
+def make_prefill(device, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(B, L, D, device=device, dtype=torch.bfloat16, generator=g)
+    w = (torch.rand(D, W, device=device, generator=g) - 0.5).to(torch.bfloat16)
+    b = (torch.randn(D, device=device, generator=g) * 0.1).to(torch.bfloat16)
+    return x, w, b
+
+
+def run_headline(args, rank, world, device):
+    import causal_conv1d_cute as C
+
+    x, w, bias = make_prefill(device, 1234 + rank)
+    xv = x.transpose(1, 2)  # (B, D, L) channel-last view
+    out = torch.empty(B, L, D, device=device, dtype=torch.bfloat16).transpose(1, 2)
+
+    def step():
+        C.causal_conv1d_fn(xv, w, bias, "silu", out=out)
+
+    for _ in range(args.warmup):
+        step()
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(device.index)
+    with sampler:
+        total_ms, per = time_launches(step, args.steps)
+    total_ms = allreduce_max(total_ms, world, device)
+    avg_launch_ms = statistics.mean(per)
+
+    # End to end through the public API: pinned host input in, result back to pinned host memory.
+    xh = torch.empty(B, L, D, dtype=torch.bfloat16, pin_memory=True)
+    xh.copy_(x)
+    oh = torch.empty(B, L, D, dtype=torch.bfloat16, pin_memory=True)
+    xd = torch.empty_like(x)
+
+    def e2e_step():
+        xd.copy_(xh, non_blocking=True)
+        y = C.causal_conv1d_fn(xd.transpose(1, 2), w, bias, "silu")
+        oh.copy_(y.transpose(1, 2), non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    e2e_steps = max(3, min(args.steps, 10))
+    dist_barrier(world)
+    torch.cuda.synchronize()
+    e2e_ms, _ = time_launches(e2e_step, e2e_steps)
+    e2e_ms = allreduce_max(e2e_ms, world, device)
+    torch.cuda.synchronize()
+    # The result read back must equal the device result.
+    assert torch.equal(oh.to(device), out.transpose(1, 2))
+
+    value = HEADLINE_BYTES * world * args.steps / (total_ms / 1e3) / 1e9
+    e2e_value = HEADLINE_BYTES * world * e2e_steps / (e2e_ms / 1e3) / 1e9
+    achieved = HEADLINE_BYTES / (avg_launch_ms / 1e3) / 1e9
+    peak, peak_kind = peaks()
+    traffic = profiled_traffic("fwd_channel_last_kernel")
+    return {
+        "value": value,
+        "ms_per_step": total_ms / args.steps,
+        "e2e": {
+            "value": e2e_value,
+            "unit": "GB/s",
+            "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+            "d2h_bytes_per_step": oh.numel() * oh.element_size(),
+            "ms_per_step": e2e_ms / e2e_steps,
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": traffic,
+            "peak_source": f"{peak_kind} hbm_gbs (copy, burst)",
+            "kernel": "fwd_channel_last_kernel",
+            "algorithmic_bytes_per_launch": HEADLINE_BYTES,
+            "avg_launch_us": avg_launch_ms * 1e3,
+        },
+        "clocks": sampler.summary(),
+        "gpu_launches": args.steps,
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# Other BASELINE paths (N = 1)
+# ---------------------------------------------------------------------------------------------
+
+
+def _stats(per_ms):
+    per = sorted(per_ms)
+    return statistics.median(per) * 1e3
+
+
+def run_paths(device, reps=200):
+    import causal_conv1d_cute as C
+
+    g = torch.Generator(device=device).manual_seed(7)
+    bf = torch.bfloat16
+    res = {}
+    w4 = (torch.rand(D, 4, device=device, generator=g) - 0.5).to(bf)
+    bias = (torch.randn(D, device=device, generator=g) * 0.1).to(bf)
+
+    # Config 3: single-token indexed decode, B=256, 1024-slot cache.
+    Bd, slots = 256, 1024
+    x = torch.randn(Bd, D, device=device, generator=g).to(bf)
+    cache = torch.randn(slots, D, 3, device=device, generator=g).to(bf)
+    idx = torch.randperm(slots, device=device, generator=g)[:Bd].to(torch.int32)
+    nbytes = 4 * Bd * D * 2 + 2 * Bd * D * 3 * 2 + D * 4 * 2 + D * 2 + Bd * 4
+    f = lambda: C.causal_conv1d_update(x, cache, w4, bias, "silu", idx)  # noqa: E731
+    for _ in range(10):
+        f()
+    _, cold = time_launches(f, reps, flush=flush_l2)
+    _, warm = time_launches(f, reps)
+    res["decode_indexed_b256"] = {"us_cold": _stats(cold), "us_warm": _stats(warm),
+                                  "bytes": nbytes, "gbs_cold": nbytes / (_stats(cold) * 1e3)}
+
+    # Config 3 ring variant: ring (256, 3, 8192), seen ~U[1, 8192].
+    ring = torch.randn(Bd, 3, D, device=device, generator=g).to(bf)
+    seen = torch.randint(1, 8193, (Bd,), device=device, generator=g, dtype=torch.int32)
+    nbytes = 2 * Bd * D * 2 + 3 * Bd * D * 2 + Bd * D * 2 + D * 4 * 2 + D * 2 + Bd * 4
+    f = lambda: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen)  # noqa: E731
+    for _ in range(10):
+        f()
+    _, cold = time_launches(f, reps, flush=flush_l2)
+    _, warm = time_launches(f, reps)
+    res["decode_ring_b256"] = {"us_cold": _stats(cold), "us_warm": _stats(warm), "bytes": nbytes,
+                               "gbs_cold": nbytes / (_stats(cold) * 1e3)}
+
+    # Config 4: spec-decode verify, B=64, 4 steps, dense per-step states.
+    Bs, S = 64, 4
+    xs = torch.randn(Bs, S, D, device=device, generator=g).to(bf).transpose(1, 2)
+    st = torch.randn(Bs, D, 3, device=device, generator=g).to(bf)
+    inter = torch.empty(Bs, S, D, 3, device=device, dtype=bf)
+    perm = torch.randperm(Bs, device=device, generator=g).to(torch.int32)
+    nbytes = 2 * Bs * S * D * 2 + 2 * Bs * D * 3 * 2 + Bs * S * D * 3 * 2 + D * 4 * 2 + D * 2 + 2 * Bs * 4
+    f = lambda: C.causal_conv1d_update(xs, st, w4, bias, "silu", perm, -1, inter, perm)  # noqa: E731
+    for _ in range(10):
+        f()
+    _, cold = time_launches(f, reps, flush=flush_l2)
+    _, warm = time_launches(f, reps)
+    res["spec_decode_b64_s4"] = {"us_cold": _stats(cold), "us_warm": _stats(warm), "bytes": nbytes,
+                                 "gbs_cold": nbytes / (_stats(cold) * 1e3)}
+
+    # Config 5: varlen, 32 lognormal(7, 1) lengths clipped to [1, 8192], token-major x.
+    rng = np.random.default_rng(0)
+    lens = np.clip(np.round(rng.lognormal(7, 1, 32)), 1, 8192).astype(np.int64)
+    T = int(lens.sum())
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=device, dtype=torch.int32)
+    cidx = torch.from_numpy(rng.choice(512, 32, replace=False).astype(np.int32)).to(device)
+    hinit = torch.from_numpy(rng.random(32) < 0.5).to(device)
+    xv = torch.randn(T, D, device=device, generator=g).to(bf)
+    for Wv in (2, 3, 4, 8):
+        wv = (torch.rand(D, Wv, device=device, generator=g) - 0.5).to(bf)
+        states = torch.randn(512, D, Wv - 1, device=device, generator=g).to(bf)
+        nh = int(hinit.sum())
+        nbytes = 2 * D * T * 2 + D * (Wv - 1) * 2 * (32 + nh) + 4 * 33 + 4 * 32 + 32 + D * Wv * 2
+        f = lambda: C.causal_conv1d_varlen_fn(xv.t(), wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
+        for _ in range(5):
+            f()
+        _, per = time_launches(f, 50)
+        us = _stats(per)
+        res[f"varlen_w{Wv}"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3), "tokens": T}
+    return res
+
+
+# ---------------------------------------------------------------------------------------------
+# CPU baseline (the C port of the reference's fallback)
+# ---------------------------------------------------------------------------------------------
+
+
+def cpu_baseline(min_seconds=10.0):
+    from oracle import native
+
+    rng = np.random.default_rng(0)
+    Ls = 256
+    x = (rng.standard_normal((1, Ls, D)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    w = (rng.uniform(-0.5, 0.5, (D, W)).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    b = (rng.standard_normal(D).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    native.fwd_cl_bf16(x, w, b, True)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        native.fwd_cl_bf16(x, w, b, True)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    sample_bytes = 2 * Ls * D * E + D * W * E + D * E
+    return {
+        "value": sample_bytes * n / el / 1e9,
+        "unit": "GB/s",
+        "cores": native.threads(),
+        "kind": "port",
+        "sample": f"{n} calls of batch 1 x {Ls} tokens x {D} channels (W=4, bias, SiLU) of the "
+                  f"config-2 workload, {el:.1f} s, oracle/cc1d_oracle.c with OpenMP",
+    }
+
+
+# ---------------------------------------------------------------------------------------------
+# Distributed plumbing
+# ---------------------------------------------------------------------------------------------
+
+
+def dist_barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def allreduce_max(v, world, device):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sharded_check(rank, world, device):
+    """All-gather a sample of every rank's channel slice and compare with the unsharded run."""
+    import causal_conv1d_cute as C
+
+    Ls, Dg = 128, D * world
+    g = torch.Generator(device=device).manual_seed(99)
+    xg = torch.randn(1, Ls, Dg, device=device, generator=g).to(torch.bfloat16)
+    wg = (torch.rand(Dg, W, device=device, generator=g) - 0.5).to(torch.bfloat16)
+    bg = (torch.randn(Dg, device=device, generator=g) * 0.1).to(torch.bfloat16)
+    lo, hi = rank * D, (rank + 1) * D
+    mine = C.causal_conv1d_fn(xg[:, :, lo:hi].transpose(1, 2), wg[lo:hi], bg[lo:hi], "silu")
+    mine = mine.transpose(1, 2).contiguous()
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    torch.distributed.all_gather(parts, mine)
+    ok = True
+    if rank == 0:
+        full = C.causal_conv1d_fn(xg.transpose(1, 2), wg, bg, "silu").transpose(1, 2)
+        ok = torch.equal(torch.cat(parts, dim=2), full)
+    flag = torch.tensor([1 if ok else 0], device=device)
+    torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
+    return bool(flag.item())
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    n = max(world, 1)
+    config = {
+        "workload": "prefill_bf16_channel_last (BASELINE config 2)",
+        "batch": B, "seqlen": L, "dim_per_gpu": D, "dim_global": D * n, "width": W,
+        "activation": "silu", "bias": True,
+        "layout": "x stored (batch, seqlen, dim), passed as its (batch, dim, seqlen) view",
+        "l2": "inputs (512 MiB per GPU) larger than L2 (126 MB); no flush",
+        "parallelism": f"channel-sliced tp{n}: each rank owns {D} channels, no collective in the path",
+    }
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        from oracle import native
+
+        steps = max(1, args.steps if args.steps < 50 else 20)
+        per_step = []
+        for i in range(min(args.warmup, 2) + steps):
+            t0 = time.perf_counter()
+            cb = cpu_baseline(min_seconds=0.5)
+            if i >= min(args.warmup, 2):
+                per_step.append(cb["value"])
+        v = statistics.median(per_step)
+        line = {
+            "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": n,
+            "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": native.threads(), "kind": "port",
+                             "sample": "each step: batch 1 x 256 tokens x 8192 channels of config 2 "
+                                       "for >= 0.5 s, oracle/cc1d_oracle.c (C port of the reference's "
+                                       "fallback.py) with OpenMP"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line))
+        return
+
+    if world > 1:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    head = run_headline(args, rank, world, device)
+    line = {
+        "metric": METRIC,
+        "value": head["value"],
+        "unit": "GB/s",
+        "n_gpus": n,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": config,
+        "e2e": head["e2e"],
+        "roofline": head["roofline"],
+        "clocks": head["clocks"],
+        "gpu_launches": head["gpu_launches"],
+    }
+    if world > 1:
+        line["sharded_check"] = "bit-identical" if sharded_check(rank, world, device) else "MISMATCH"
+    if rank == 0 and n == 1:
+        if not args.no_paths:
+            line["paths"] = run_paths(device)
+        line["cpu_baseline"] = cpu_baseline()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,177 @@
+"""Tensor-level calls into libcc1d.so.
+
+Each function passes data pointers, element strides and sizes of already-validated CUDA tensors to
+one C entry point, on the current stream of the tensors' device. No host synchronisation, no
+allocation: outputs are allocated by the caller. The C side picks the kernel variant for the
+layout it is given.
+
+Device status. When checks are enabled (set_device_checks(True)), every call passes a per-device
+int32 status word that kernels OR a bit into when they skip an index outside the caches (a slot
+outside the state cache, sequence bounds outside the packed tokens). device_status() reads and
+clears it. Checks are off by default so that no call allocates anything.
+"""
+
+import torch
+
+from . import _lib
+from ._lib import check, dtype_code, load
+
+_checks = False
+_status = {}
+
+
+def set_device_checks(enabled=True):
+    """Turn the device-side index checks' status word on or off for later calls."""
+    global _checks
+    _checks = bool(enabled)
+
+
+def device_status(device=None, clear=True):
+    """Return the OR of the CC1D_DEV_* bits reported on device since the last clear (syncs)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    t = _status.get(dev.index)
+    if t is None:
+        return 0
+    v = int(t.item())
+    if clear:
+        t.zero_()
+    return v
+
+
+def _status_ptr(device):
+    if not _checks:
+        return None
+    t = _status.get(device.index)
+    if t is None:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        t = _status[device.index] = torch.zeros(1, dtype=torch.int32, device=device)
+    return t.data_ptr()
+
+
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _stream(device):
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def fwd(x, weight, bias, silu, out):
+    """out[b, c, t] for x, out of shape (batch, dim, seqlen), any strides (cc1d_fwd)."""
+    lib = load()
+    B, D, L = x.shape
+    check(
+        lib.cc1d_fwd(
+            x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
+            weight.data_ptr(), weight.stride(0), weight.stride(1),
+            _ptr(bias), 0 if bias is None else bias.stride(0),
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+            B, D, L, weight.shape[1], dtype_code(x.dtype), int(bool(silu)), _stream(x.device),
+        )
+    )
+    return out
+
+
+def update(x3, state, weight, bias, silu, out3, idx, pad, inter, iidx):
+    """Decode of x3 (batch, dim, steps) into out3 of the same shape (cc1d_update).
+
+    state is (slots, dim, state_len); inter, when given, is (inter_slots, steps, dim, W-1).
+    idx / iidx are int32 CUDA tensors or None.
+    """
+    lib = load()
+    B, D, L = x3.shape
+    if inter is None:
+        ip, ist, inslots = None, (0, 0, 0, 0), 0
+    else:
+        ip, ist, inslots = inter.data_ptr(), inter.stride(), inter.shape[0]
+    check(
+        lib.cc1d_update(
+            x3.data_ptr(), x3.stride(0), x3.stride(1), x3.stride(2),
+            state.data_ptr(), state.stride(0), state.stride(1), state.stride(2),
+            state.shape[2], state.shape[0],
+            weight.data_ptr(), weight.stride(0), weight.stride(1),
+            _ptr(bias), 0 if bias is None else bias.stride(0),
+            out3.data_ptr(), out3.stride(0), out3.stride(1), out3.stride(2),
+            _ptr(idx), int(pad),
+            ip, ist[0], ist[1], ist[2], ist[3], inslots, _ptr(iidx),
+            B, D, L, weight.shape[1], dtype_code(x3.dtype), int(bool(silu)),
+            _status_ptr(x3.device), _stream(x3.device),
+        )
+    )
+    return out3
+
+
+def update_ring(x, ring, weight, bias, silu, out, seen, idx, pad):
+    """Ring decode of x (batch, dim) against ring (slots, W-1, dim) (cc1d_update_ring)."""
+    lib = load()
+    B, D = x.shape
+    check(
+        lib.cc1d_update_ring(
+            x.data_ptr(), x.stride(0), x.stride(1),
+            ring.data_ptr(), ring.stride(0), ring.stride(1), ring.stride(2), ring.shape[0],
+            weight.data_ptr(), weight.stride(0), weight.stride(1),
+            _ptr(bias), 0 if bias is None else bias.stride(0),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            seen.data_ptr(), _ptr(idx), int(pad),
+            B, D, weight.shape[1], dtype_code(x.dtype), int(bool(silu)),
+            _status_ptr(x.device), _stream(x.device),
+        )
+    )
+    return out
+
+
+def varlen(x, weight, bias, silu, out, qsl, cidx, hinit, states, pad):
+    """Packed prefill of x (dim, ntokens) into out (dim, ntokens) (cc1d_varlen).
+
+    qsl int32 (nseq + 1,); cidx int32 or None; hinit uint8 or None; states (slots, dim, W-1)
+    or None.
+    """
+    lib = load()
+    D, T = x.shape
+    if states is None:
+        sp, ss, nslots = None, (0, 0, 0), 0
+    else:
+        sp, ss, nslots = states.data_ptr(), states.stride(), states.shape[0]
+    check(
+        lib.cc1d_varlen(
+            x.data_ptr(), x.stride(0), x.stride(1),
+            weight.data_ptr(), weight.stride(0), weight.stride(1),
+            _ptr(bias), 0 if bias is None else bias.stride(0),
+            out.data_ptr(), out.stride(0), out.stride(1),
+            qsl.data_ptr(), qsl.numel() - 1, T, _ptr(cidx), _ptr(hinit),
+            sp, ss[0], ss[1], ss[2], nslots, int(pad),
+            D, weight.shape[1], dtype_code(x.dtype), int(bool(silu)),
+            _status_ptr(x.device), _stream(x.device),
+        )
+    )
+    return out
+
+
+def update_unpack(qkvz, ba, state, weight, bias, out, z, b, a, idx, heads, silu, pad):
+    """Fused Gated DeltaNet decode step (cc1d_update_unpack)."""
+    lib = load()
+    B = qkvz.shape[0]
+    D, W = weight.shape
+    zdim = qkvz.shape[1] - D
+    check(
+        lib.cc1d_update_unpack(
+            qkvz.data_ptr(), qkvz.stride(0), ba.data_ptr(), ba.stride(0),
+            state.data_ptr(), state.shape[0], weight.data_ptr(), _ptr(bias),
+            out.data_ptr(), z.data_ptr(), b.data_ptr(), a.data_ptr(),
+            idx.data_ptr(), int(pad), B, D, zdim, int(heads), W,
+            dtype_code(qkvz.dtype), dtype_code(ba.dtype), int(bool(silu)), _stream(qkvz.device),
+        )
+    )
+    return out, z, b, a
+
+
+__all__ = [
+    "device_status", "fwd", "set_device_checks", "update", "update_ring", "update_unpack",
+    "varlen", "_lib",
+]

@@ -1,0 +1,221 @@
+// extern "C" entry points of libcc1d.so (declared in include/cc1d.h). Each one validates its
+// arguments on the host, returns a status code instead of throwing, and enqueues one kernel on
+// the caller's stream. Nothing is allocated and nothing is synchronised.
+#include <stdarg.h>
+#include <stdio.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+cc1d_status_t fail(cc1d_status_t code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+cc1d_status_t ok() {
+    g_last_error[0] = '\0';
+    return CC1D_OK;
+}
+
+cc1d_status_t from_cuda(cudaError_t err, const char* what) {
+    if (err == cudaSuccess) return ok();
+    return fail(CC1D_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+cc1d_status_t check_common(int32_t width, int32_t dtype) {
+    if (dtype != CC1D_BF16 && dtype != CC1D_F16 && dtype != CC1D_F32)
+        return fail(CC1D_ERR_DTYPE, "dtype %d is not bf16 (0), fp16 (1) or fp32 (2)", dtype);
+    if (width < 2 || width > 8) return fail(CC1D_ERR_WIDTH, "kernel width %d is outside 2..8", width);
+    return CC1D_OK;
+}
+
+// Make the stream's device current on this thread, so a launch from any host thread lands on
+// the device that owns the stream (the legacy default stream keeps the current device).
+cc1d_status_t bind_stream(void* stream) {
+    if (stream == nullptr) return CC1D_OK;
+    int dev = -1, cur = -1;
+    cudaError_t err = cudaStreamGetDevice((cudaStream_t)stream, &dev);
+    if (err != cudaSuccess) return from_cuda(err, "cudaStreamGetDevice");
+    err = cudaGetDevice(&cur);
+    if (err != cudaSuccess) return from_cuda(err, "cudaGetDevice");
+    if (cur != dev) {
+        err = cudaSetDevice(dev);
+        if (err != cudaSuccess) return from_cuda(err, "cudaSetDevice");
+    }
+    return CC1D_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t cc1d_abi_version(void) { return 1; }
+
+const char* cc1d_status_string(cc1d_status_t code) {
+    switch (code) {
+        case CC1D_OK: return "ok";
+        case CC1D_ERR_INVALID: return "invalid argument";
+        case CC1D_ERR_DTYPE: return "unsupported dtype";
+        case CC1D_ERR_WIDTH: return "unsupported kernel width";
+        case CC1D_ERR_LAYOUT: return "unsupported tensor layout";
+        case CC1D_ERR_CUDA: return "CUDA launch failed";
+        default: return "unknown status";
+    }
+}
+
+const char* cc1d_last_error(void) { return g_last_error; }
+
+cc1d_status_t cc1d_fwd(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_sl,
+                       const void* weight, int64_t w_sd, int64_t w_sk,
+                       const void* bias, int64_t bias_s,
+                       void* out, int64_t o_sb, int64_t o_sd, int64_t o_sl,
+                       int64_t batch, int64_t dim, int64_t seqlen, int32_t width,
+                       int32_t dtype, int32_t silu, void* stream) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (batch < 0 || dim < 0 || seqlen < 0)
+        return fail(CC1D_ERR_INVALID, "negative size (batch %lld, dim %lld, seqlen %lld)",
+                    (long long)batch, (long long)dim, (long long)seqlen);
+    if (batch == 0 || dim == 0 || seqlen == 0) return ok();
+    if (x == nullptr || weight == nullptr || out == nullptr)
+        return fail(CC1D_ERR_INVALID, "x, weight and out must not be NULL");
+    cc1d::FwdArgs a{x, x_sb, x_sd, x_sl, weight, w_sd, w_sk, bias, bias_s,
+                    out, o_sb, o_sd, o_sl, batch, dim, seqlen, silu != 0};
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_fwd(a, width, dtype, (cudaStream_t)stream), "cc1d_fwd");
+}
+
+cc1d_status_t cc1d_update(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_st,
+                          void* state, int64_t s_slot, int64_t s_sd, int64_t s_sk,
+                          int64_t state_len, int64_t nslots,
+                          const void* weight, int64_t w_sd, int64_t w_sk,
+                          const void* bias, int64_t bias_s,
+                          void* out, int64_t o_sb, int64_t o_sd, int64_t o_st,
+                          const int32_t* state_indices, int32_t pad_slot_id,
+                          void* inter, int64_t i_slot, int64_t i_st, int64_t i_sd, int64_t i_sk,
+                          int64_t inter_nslots, const int32_t* inter_indices,
+                          int64_t batch, int64_t dim, int32_t steps, int32_t width,
+                          int32_t dtype, int32_t silu, int32_t* dev_status, void* stream) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (batch < 0 || dim < 0 || steps < 1)
+        return fail(CC1D_ERR_INVALID, "bad sizes (batch %lld, dim %lld, steps %d)",
+                    (long long)batch, (long long)dim, steps);
+    if (state_len < width - 1)
+        return fail(CC1D_ERR_INVALID, "state length %lld is shorter than width - 1 = %d",
+                    (long long)state_len, width - 1);
+    if (batch == 0 || dim == 0) return ok();
+    if (x == nullptr || weight == nullptr || out == nullptr || state == nullptr)
+        return fail(CC1D_ERR_INVALID, "x, state, weight and out must not be NULL");
+    if (state_indices == nullptr && nslots < batch)
+        return fail(CC1D_ERR_INVALID, "without state indices the cache needs >= %lld slots, has %lld",
+                    (long long)batch, (long long)nslots);
+    if (inter != nullptr && inter_nslots < 1)
+        return fail(CC1D_ERR_INVALID, "the per-step state cache has no slots");
+    cc1d::UpdArgs a{x, x_sb, x_sd, x_st, state, s_slot, s_sd, s_sk, state_len, nslots,
+                    weight, w_sd, w_sk, bias, bias_s, out, o_sb, o_sd, o_st,
+                    state_indices, pad_slot_id, inter, i_slot, i_st, i_sd, i_sk, inter_nslots,
+                    inter_indices, batch, dim, steps, silu != 0, dev_status};
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_update(a, width, dtype, (cudaStream_t)stream), "cc1d_update");
+}
+
+cc1d_status_t cc1d_update_ring(const void* x, int64_t x_sb, int64_t x_sd,
+                               void* ring, int64_t r_slot, int64_t r_sk, int64_t r_sd,
+                               int64_t nslots,
+                               const void* weight, int64_t w_sd, int64_t w_sk,
+                               const void* bias, int64_t bias_s,
+                               void* out, int64_t o_sb, int64_t o_sd,
+                               const int32_t* cache_seqlens, const int32_t* state_indices,
+                               int32_t pad_slot_id, int64_t batch, int64_t dim, int32_t width,
+                               int32_t dtype, int32_t silu, int32_t* dev_status, void* stream) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (batch < 0 || dim < 0)
+        return fail(CC1D_ERR_INVALID, "negative size (batch %lld, dim %lld)", (long long)batch,
+                    (long long)dim);
+    if (batch == 0 || dim == 0) return ok();
+    if (x == nullptr || ring == nullptr || weight == nullptr || out == nullptr ||
+        cache_seqlens == nullptr)
+        return fail(CC1D_ERR_INVALID, "x, ring, weight, out and cache_seqlens must not be NULL");
+    if (state_indices == nullptr && nslots < batch)
+        return fail(CC1D_ERR_INVALID, "without state indices the ring needs >= %lld slots, has %lld",
+                    (long long)batch, (long long)nslots);
+    cc1d::RingArgs a{x, x_sb, x_sd, ring, r_slot, r_sk, r_sd, nslots, weight, w_sd, w_sk,
+                     bias, bias_s, out, o_sb, o_sd, cache_seqlens, state_indices, pad_slot_id,
+                     batch, dim, silu != 0, dev_status};
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_ring(a, width, dtype, (cudaStream_t)stream), "cc1d_update_ring");
+}
+
+cc1d_status_t cc1d_varlen(const void* x, int64_t x_sd, int64_t x_st,
+                          const void* weight, int64_t w_sd, int64_t w_sk,
+                          const void* bias, int64_t bias_s,
+                          void* out, int64_t o_sd, int64_t o_st,
+                          const int32_t* query_start_loc, int64_t nseq, int64_t ntokens,
+                          const int32_t* cache_indices, const uint8_t* has_initial_state,
+                          void* conv_states, int64_t s_slot, int64_t s_sd, int64_t s_sk,
+                          int64_t nslots, int32_t pad_slot_id, int64_t dim, int32_t width,
+                          int32_t dtype, int32_t silu, int32_t* dev_status, void* stream) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (nseq < 0 || ntokens < 0 || dim < 0)
+        return fail(CC1D_ERR_INVALID, "negative size (nseq %lld, ntokens %lld, dim %lld)",
+                    (long long)nseq, (long long)ntokens, (long long)dim);
+    if (nseq == 0 || ntokens == 0 || dim == 0) return ok();
+    if (ntokens > INT32_MAX)
+        return fail(CC1D_ERR_INVALID, "%lld tokens exceed the int32 range of query_start_loc",
+                    (long long)ntokens);
+    if (x == nullptr || weight == nullptr || out == nullptr || query_start_loc == nullptr)
+        return fail(CC1D_ERR_INVALID, "x, weight, out and query_start_loc must not be NULL");
+    if (conv_states != nullptr && nslots < 1)
+        return fail(CC1D_ERR_INVALID, "the conv state cache has no slots");
+    cc1d::VarArgs a{x, x_sd, x_st, weight, w_sd, w_sk, bias, bias_s, out, o_sd, o_st,
+                    query_start_loc, nseq, ntokens, cache_indices, has_initial_state,
+                    conv_states, s_slot, s_sd, s_sk, nslots, pad_slot_id, dim, silu != 0,
+                    dev_status};
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_varlen(a, width, dtype, (cudaStream_t)stream), "cc1d_varlen");
+}
+
+cc1d_status_t cc1d_update_unpack(const void* qkvz, int64_t q_sb, const void* ba, int64_t ba_sb,
+                                 void* state, int64_t nslots,
+                                 const void* weight, const void* bias,
+                                 void* out, void* z, void* b, void* a,
+                                 const int32_t* state_indices, int32_t pad_slot_id,
+                                 int64_t batch, int64_t dim, int64_t zdim, int64_t heads,
+                                 int32_t width, int32_t dtype, int32_t gdtype, int32_t silu,
+                                 void* stream) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (gdtype != CC1D_BF16 && gdtype != CC1D_F16 && gdtype != CC1D_F32)
+        return fail(CC1D_ERR_DTYPE, "gate dtype %d is not bf16, fp16 or fp32", gdtype);
+    if (batch < 0 || dim < 0 || zdim < 0 || heads < 0)
+        return fail(CC1D_ERR_INVALID, "negative size");
+    if (batch == 0) return ok();
+    if (batch > 65535) return fail(CC1D_ERR_INVALID, "batch %lld exceeds 65535", (long long)batch);
+    if (!qkvz || !ba || !state || !weight || !out || !z || !b || !a || !state_indices)
+        return fail(CC1D_ERR_INVALID, "a required pointer is NULL");
+    const int64_t e = dtype == CC1D_F32 ? 4 : 2;
+    const int64_t V = 16 / e;
+    const int64_t ge = gdtype == CC1D_F32 ? 4 : 2;
+    if (dim % V || zdim % V || (q_sb * e) % 16 || !cc1d::host_aligned16(qkvz) ||
+        !cc1d::host_aligned16(state) || !cc1d::host_aligned16(weight) ||
+        !cc1d::host_aligned16(out) || !cc1d::host_aligned16(z) ||
+        (bias != nullptr && !cc1d::host_aligned16(bias)) || q_sb < dim + zdim ||
+        ba_sb < 2 * heads || ((uintptr_t)ba % ge) != 0)
+        return fail(CC1D_ERR_LAYOUT,
+                    "fused decode needs dim and zdim multiples of %lld, 16-byte aligned rows and "
+                    "contiguous state, weight and outputs",
+                    (long long)V);
+    cc1d::UnpackArgs args{qkvz, q_sb, ba, ba_sb, state, nslots, weight, bias, out, z, b, a,
+                          state_indices, pad_slot_id, batch, dim, zdim, heads, (int)ge,
+                          silu != 0};
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_unpack(args, width, dtype, (cudaStream_t)stream),
+                     "cc1d_update_unpack");
+}
+
+}  // extern "C"

@@ -1,0 +1,280 @@
+// Shared device helpers for the depthwise causal conv1d kernels (sm_100a).
+//
+// Every kernel moves data in 16-byte vectors: V = 16 / sizeof(T) adjacent elements (8 for
+// bf16/fp16, 4 for fp32), accumulates in fp32 with the bias first and the taps in order
+// k = 0..W-1 (oldest input first), then applies SiLU and rounds to the storage dtype. This is
+// the accumulation order of the reference kernels (causal_conv1d_cute/fwd.py:217-225).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "../../include/cc1d.h"
+
+namespace cc1d {
+
+using bf16 = __nv_bfloat16;
+using f16 = __half;
+
+template <typename T>
+struct Vec {
+    static constexpr int V = 16 / (int)sizeof(T);  // elements per 16-byte vector
+};
+
+// ---------------------------------------------------------------------------------------------
+// 16-byte vector <-> fp32 lanes
+// ---------------------------------------------------------------------------------------------
+
+template <typename T>
+__device__ __forceinline__ void unpack16(const uint4& v, float* f);
+
+template <>
+__device__ __forceinline__ void unpack16<bf16>(const uint4& v, float* f) {
+    // A bf16 is the high half of an fp32: widening is a shift or a mask.
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(w[i] << 16);
+        f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+}
+
+template <>
+__device__ __forceinline__ void unpack16<f16>(const uint4& v, float* f) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 h = *reinterpret_cast<const __half2*>(&w[i]);
+        float2 p = __half22float2(h);
+        f[2 * i] = p.x;
+        f[2 * i + 1] = p.y;
+    }
+}
+
+template <>
+__device__ __forceinline__ void unpack16<float>(const uint4& v, float* f) {
+    f[0] = __uint_as_float(v.x);
+    f[1] = __uint_as_float(v.y);
+    f[2] = __uint_as_float(v.z);
+    f[3] = __uint_as_float(v.w);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack16(const float* f);
+
+template <>
+__device__ __forceinline__ uint4 pack16<bf16>(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <>
+__device__ __forceinline__ uint4 pack16<f16>(const float* f) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        __half2 h = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+        w[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <>
+__device__ __forceinline__ uint4 pack16<float>(const float* f) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                      __float_as_uint(f[3]));
+}
+
+// Element <-> fp32 for the scalar paths.
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<bf16>(bf16 v) { return __bfloat162float(v); }
+template <>
+__device__ __forceinline__ float to_f32<f16>(f16 v) { return __half2float(v); }
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float v);
+template <>
+__device__ __forceinline__ bf16 from_f32<bf16>(float v) { return __float2bfloat16_rn(v); }
+template <>
+__device__ __forceinline__ f16 from_f32<f16>(float v) { return __float2half_rn(v); }
+template <>
+__device__ __forceinline__ float from_f32<float>(float v) { return v; }
+
+// Raw element i (0..V-1) of a 16-byte vector, kept in the storage type (bit-exact copies).
+template <typename T>
+__device__ __forceinline__ T lane_of(const uint4& v, int i) {
+    return reinterpret_cast<const T*>(&v)[i];
+}
+template <typename T>
+__device__ __forceinline__ void set_lane(uint4& v, int i, T val) {
+    reinterpret_cast<T*>(&v)[i] = val;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Global memory access
+// ---------------------------------------------------------------------------------------------
+
+// Read-only data that this kernel never writes (inputs, weights): non-coherent path.
+__device__ __forceinline__ uint4 ldg16(const void* p) {
+    return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// Streamed input read once: do not keep it in L1.
+__device__ __forceinline__ uint4 ldg16_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// Data that the same kernel later overwrites (conv state caches): coherent load.
+__device__ __forceinline__ uint4 ld16(const void* p) {
+    return *reinterpret_cast<const uint4*>(p);
+}
+
+__device__ __forceinline__ void st16(void* p, const uint4& v) {
+    *reinterpret_cast<uint4*>(p) = v;
+}
+
+// Streamed output written once: evict-first so it does not displace reusable lines in L2.
+__device__ __forceinline__ void st16_stream(void* p, const uint4& v) {
+    asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+                 "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) {
+    return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Activation
+// ---------------------------------------------------------------------------------------------
+
+// Hardware tanh approximation (PTX tanh.approx.f32, sm_75+).
+__device__ __forceinline__ float tanh_approx(float x) {
+    float y;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// SiLU a * sigmoid(a). For 16-bit outputs sigmoid(a) = 0.5 * tanh(a / 2) + 0.5 evaluated with the
+// hardware approximation, written as h * tanh(h) + h with h = a / 2; its error is far below one
+// bf16/fp16 ulp. fp32 outputs use the library expf.
+template <typename T>
+__device__ __forceinline__ float silu(float a) {
+    if constexpr (std::is_same<T, float>::value) {
+        return a / (1.0f + expf(-a));
+    } else {
+        const float h = 0.5f * a;
+        return fmaf(h, tanh_approx(h), h);
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ float activate(float a, bool use_silu) {
+    return use_silu ? silu<T>(a) : a;
+}
+
+__device__ __forceinline__ void flag_status(int32_t* status, int32_t bits) {
+    if (status != nullptr) atomicOr(status, bits);
+}
+
+// ---------------------------------------------------------------------------------------------
+// Filter weights and bias of V adjacent channels, widened to fp32 registers
+// ---------------------------------------------------------------------------------------------
+
+// w[k][e] = weight[c0 + e, k]; b[e] = bias[c0 + e] (0 without bias). The weights are the caller's
+// own (dim, W) tensor read in place: when it is contiguous and 16-byte aligned (wvec) the V*W
+// elements of a channel group are W whole 16-byte vectors, otherwise they are read one by one.
+// bvec: the bias is contiguous and 16-byte aligned.
+template <typename T, int W>
+__device__ __forceinline__ void load_filter(const T* __restrict__ weight, int64_t w_sd,
+                                            int64_t w_sk, const T* __restrict__ bias,
+                                            int64_t bias_s, int64_t c0, bool wvec, bool bvec,
+                                            float (&w)[W][Vec<T>::V], float (&b)[Vec<T>::V]) {
+    constexpr int V = Vec<T>::V;
+    if (wvec) {
+        const T* base = weight + c0 * W;
+#pragma unroll
+        for (int q = 0; q < W; ++q) {
+            float f[V];
+            unpack16<T>(ldg16(base + q * V), f);
+#pragma unroll
+            for (int i = 0; i < V; ++i) {
+                const int flat = q * V + i;  // = e * W + k
+                w[flat % W][flat / W] = f[i];
+            }
+        }
+    } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e)
+#pragma unroll
+            for (int k = 0; k < W; ++k)
+                w[k][e] = to_f32<T>(__ldg(weight + (c0 + e) * w_sd + k * w_sk));
+    }
+    if (bias == nullptr) {
+#pragma unroll
+        for (int e = 0; e < V; ++e) b[e] = 0.f;
+    } else if (bvec) {
+        unpack16<T>(ldg16(bias + c0), b);
+    } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) b[e] = to_f32<T>(__ldg(bias + (c0 + e) * bias_s));
+    }
+}
+
+// Weights of one channel, for the scalar kernels.
+template <typename T, int W>
+__device__ __forceinline__ void load_filter1(const T* __restrict__ weight, int64_t w_sd,
+                                             int64_t w_sk, const T* __restrict__ bias,
+                                             int64_t bias_s, int64_t c, float (&w)[W],
+                                             float& b) {
+#pragma unroll
+    for (int k = 0; k < W; ++k) w[k] = to_f32<T>(__ldg(weight + c * w_sd + k * w_sk));
+    b = bias == nullptr ? 0.f : to_f32<T>(__ldg(bias + c * bias_s));
+}
+
+// ---------------------------------------------------------------------------------------------
+// Host-side dispatch
+// ---------------------------------------------------------------------------------------------
+
+#define CC1D_DISPATCH_WIDTH(width, ...)            \
+    switch (width) {                               \
+        case 2: { constexpr int kW = 2; __VA_ARGS__; } break; \
+        case 3: { constexpr int kW = 3; __VA_ARGS__; } break; \
+        case 4: { constexpr int kW = 4; __VA_ARGS__; } break; \
+        case 5: { constexpr int kW = 5; __VA_ARGS__; } break; \
+        case 6: { constexpr int kW = 6; __VA_ARGS__; } break; \
+        case 7: { constexpr int kW = 7; __VA_ARGS__; } break; \
+        case 8: { constexpr int kW = 8; __VA_ARGS__; } break; \
+        default: break;                            \
+    }
+
+#define CC1D_DISPATCH_DTYPE(dtype, ...)                              \
+    switch (dtype) {                                                 \
+        case CC1D_BF16: { using T = ::cc1d::bf16; __VA_ARGS__; } break; \
+        case CC1D_F16: { using T = ::cc1d::f16; __VA_ARGS__; } break;   \
+        case CC1D_F32: { using T = float; __VA_ARGS__; } break;         \
+        default: break;                                              \
+    }
+
+__host__ __device__ inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+inline bool host_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace cc1d

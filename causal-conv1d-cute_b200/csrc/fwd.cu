@@ -1,0 +1,306 @@
+// Prefill over dense batched sequences (replaces causal_conv1d_cute/fwd.py).
+//
+// Three kernels, chosen by layout in launch_fwd:
+//   fwd_channel_last   (B, L, D) storage, token rows of D adjacent channels (x_sd == 1): every
+//                      thread owns one 16-byte vector of channels and walks a strip of tokens,
+//                      keeping the W-1 most recent inputs in registers. The strip re-reads only
+//                      the W-1 rows before it, which its neighbour strip has just pulled into L2.
+//   fwd_channel_first  (B, D, L) contiguous storage: the tensor is one flat stream; every lane of
+//                      a warp owns 8 consecutive elements and receives the W-1 elements before
+//                      them from the lane to its left by a warp shuffle, so HBM is read once.
+//   fwd_generic        any other strides, one channel per thread (correctness path).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cc1d {
+
+namespace {
+
+constexpr int kClThreads = 128;
+constexpr int kCfThreads = 256;
+constexpr int kGenThreads = 256;
+
+// One output vector from the fp32 window h (oldest first) and the new input xv; shifts xv into
+// the window afterwards.
+template <typename T, int W>
+__device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const float* xv,
+                                          const float (&w)[W][Vec<T>::V],
+                                          const float (&bv)[Vec<T>::V], bool use_silu,
+                                          float* o) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+        float acc = bv[e];
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
+        acc = fmaf(xv[e], w[K][e], acc);
+        o[e] = activate<T>(acc, use_silu);
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k)
+#pragma unroll
+        for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
+#pragma unroll
+    for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
+}
+
+template <typename T, int W, int U>
+__global__ void __launch_bounds__(kClThreads)
+    fwd_channel_last_kernel(const FwdArgs a, int strip, int nstrips, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    const int64_t nvec = a.D / V;
+    const int64_t j = (int64_t)blockIdx.x * kClThreads + threadIdx.x;
+    if (j >= nvec) return;
+    const int64_t c0 = j * V;
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = a.silu != 0;
+    const int64_t units = (int64_t)nstrips * a.B;
+    for (int64_t u = blockIdx.y; u < units; u += gridDim.y) {
+        const int64_t b = u / nstrips;
+        const int64_t t0 = (u - b * nstrips) * (int64_t)strip;
+        const int64_t t1 = min(t0 + strip, a.L);
+        const T* xb = (const T*)a.x + b * a.x_sb + c0;
+        T* ob = (T*)a.out + b * a.o_sb + c0;
+        float h[K][V];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int64_t t = t0 - K + k;
+            if (t >= 0) {
+                unpack16<T>(ldg16(xb + t * a.x_sl), h[k]);
+            } else {
+#pragma unroll
+                for (int e = 0; e < V; ++e) h[k][e] = 0.f;
+            }
+        }
+        int64_t t = t0;
+        for (; t + U <= t1; t += U) {
+            uint4 r[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i) r[i] = ldg16_stream(xb + (t + i) * a.x_sl);
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+                float xv[V], o[V];
+                unpack16<T>(r[i], xv);
+                conv_step<T, W>(h, xv, w, bv, use_silu, o);
+                st16_stream(ob + (t + i) * a.o_sl, pack16<T>(o));
+            }
+        }
+        for (; t < t1; ++t) {
+            float xv[V], o[V];
+            unpack16<T>(ldg16_stream(xb + t * a.x_sl), xv);
+            conv_step<T, W>(h, xv, w, bv, use_silu, o);
+            st16_stream(ob + t * a.o_sl, pack16<T>(o));
+        }
+    }
+}
+
+// Flat-stream kernel for contiguous (B, D, L) with L >= 8. Element f sits at row f / L (channel
+// (f / L) % D) and position t = f % L; tap k of its output reads element f - (W-1) + k when that
+// lies in the same row (t >= W-1-k), zero otherwise. A lane's 8 elements straddle at most one
+// row boundary, so at most two channels' weights are needed per vector.
+template <typename T, int W>
+__global__ void __launch_bounds__(kCfThreads)
+    fwd_channel_first_kernel(const FwdArgs a, int64_t total, int iters) {
+    constexpr int K = W - 1;
+    constexpr int EPT = 8;
+    constexpr int PER = 16 / (int)sizeof(T);
+    constexpr int NV = EPT / PER;
+    const unsigned FULL = 0xffffffffu;
+    const int lane = threadIdx.x & 31;
+    const int64_t gw = ((int64_t)blockIdx.x * kCfThreads + threadIdx.x) >> 5;
+    const int64_t base = gw * (int64_t)iters * 256;
+    if (base >= total) return;  // warp-uniform
+    const T* x = (const T*)a.x;
+    T* out = (T*)a.out;
+    const T* wt = (const T*)a.w;
+    const T* bs = (const T*)a.bias;
+    const int64_t L = a.L, D = a.D;
+    const bool use_silu = a.silu != 0;
+
+    int64_t f = base + lane * EPT;
+    int64_t row = f / L;
+    int64_t t = f - row * L;
+    int64_t c = row % D;
+
+    float carry[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int64_t p = base - K + k;
+        carry[k] = (lane == 0 && p >= 0) ? to_f32<T>(x[p]) : 0.f;
+    }
+    int64_t wc = -1;
+    float w0[W], b0 = 0.f;
+    for (int it = 0; it < iters; ++it) {
+        f = base + (int64_t)it * 256 + lane * EPT;
+        float xv[EPT];
+        const bool full = f + EPT <= total;
+        if (full) {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) unpack16<T>(ldg16_stream(x + f + v * PER), xv + v * PER);
+        } else {
+#pragma unroll
+            for (int e = 0; e < EPT; ++e) xv[e] = (f + e < total) ? to_f32<T>(x[f + e]) : 0.f;
+        }
+        float win[K + EPT];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const float up = __shfl_up_sync(FULL, xv[EPT - K + k], 1);
+            const float last = __shfl_sync(FULL, xv[EPT - K + k], 31);
+            win[k] = lane == 0 ? carry[k] : up;
+            carry[k] = last;
+        }
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) win[K + e] = xv[e];
+        if (f < total) {
+            if (c != wc) {
+                load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c, w0, b0);
+                wc = c;
+            }
+            float w1[W], b1 = 0.f;
+            const bool straddle = t + EPT > L;
+            if (straddle) {
+                const int64_t c1 = (c + 1 == D) ? 0 : c + 1;
+                load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c1, w1, b1);
+            }
+            float o[EPT];
+#pragma unroll
+            for (int e = 0; e < EPT; ++e) {
+                const bool second = straddle && (t + e >= L);
+                const int64_t te = second ? t + e - L : t + e;
+                float acc = second ? b1 : b0;
+#pragma unroll
+                for (int k = 0; k < W; ++k) {
+                    const float v = (te >= K - k) ? win[e + k] : 0.f;
+                    acc = fmaf(v, second ? w1[k] : w0[k], acc);
+                }
+                o[e] = activate<T>(acc, use_silu);
+            }
+            if (full) {
+#pragma unroll
+                for (int v = 0; v < NV; ++v) st16_stream(out + f + v * PER, pack16<T>(o + v * PER));
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPT; ++e)
+                    if (f + e < total) out[f + e] = from_f32<T>(o[e]);
+            }
+        }
+        // Advance this lane by one warp stride (256 elements).
+        if (L >= 256) {
+            t += 256;
+            while (t >= L) {
+                t -= L;
+                c = (c + 1 == D) ? 0 : c + 1;
+            }
+        } else {
+            const int64_t f2 = f + 256;
+            row = f2 / L;
+            t = f2 - row * L;
+            c = row % D;
+        }
+    }
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kGenThreads)
+    fwd_generic_kernel(const FwdArgs a, int strip, int nstrips) {
+    constexpr int K = W - 1;
+    const int64_t n = a.B * a.D * nstrips;
+    const T* x = (const T*)a.x;
+    T* out = (T*)a.out;
+    const bool use_silu = a.silu != 0;
+    for (int64_t idx = (int64_t)blockIdx.x * kGenThreads + threadIdx.x; idx < n;
+         idx += (int64_t)gridDim.x * kGenThreads) {
+        const int64_t c = idx % a.D;
+        const int64_t r = idx / a.D;
+        const int64_t s = r % nstrips;
+        const int64_t b = r / nstrips;
+        float w[W], bb;
+        load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c, w, bb);
+        const int64_t t0 = s * strip;
+        const int64_t t1 = min(t0 + strip, a.L);
+        const T* xr = x + b * a.x_sb + c * a.x_sd;
+        T* orow = out + b * a.o_sb + c * a.o_sd;
+        float h[K];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int64_t t = t0 - K + k;
+            h[k] = t >= 0 ? to_f32<T>(xr[t * a.x_sl]) : 0.f;
+        }
+        for (int64_t t = t0; t < t1; ++t) {
+            const float xv = to_f32<T>(xr[t * a.x_sl]);
+            float acc = bb;
+#pragma unroll
+            for (int k = 0; k < K; ++k) acc = fmaf(h[k], w[k], acc);
+            acc = fmaf(xv, w[K], acc);
+            orow[t * a.o_sl] = from_f32<T>(activate<T>(acc, use_silu));
+#pragma unroll
+            for (int k = 0; k + 1 < K; ++k) h[k] = h[k + 1];
+            h[K - 1] = xv;
+        }
+    }
+}
+
+// Launch table for the channel-last strip walk: tokens per strip. Short strips give more
+// threads (latency hiding), long strips re-read fewer halo rows; 32 balances the two at the
+// Mamba-2 prefill shapes and is swept by the benchmark.
+int cl_strip(int64_t B, int64_t L, int64_t nvec) {
+    (void)B;
+    (void)nvec;
+    if (L <= 32) return (int)L;
+    return 32;
+}
+
+template <typename T, int W>
+cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    const int64_t e = sizeof(T);
+    const bool wvec = a.w_sd == W && a.w_sk == 1 && host_aligned16(a.w);
+    const bool bvec = a.bias != nullptr && a.bias_s == 1 && host_aligned16(a.bias);
+    const bool cl = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
+                    host_aligned16(a.out) && (a.x_sl * e) % 16 == 0 && (a.o_sl * e) % 16 == 0 &&
+                    (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0;
+    if (cl) {
+        const int64_t nvec = a.D / V;
+        const int strip = cl_strip(a.B, a.L, nvec);
+        const int nstrips = (int)ceil_div(a.L, strip);
+        const int64_t units = (int64_t)nstrips * a.B;
+        dim3 grid((unsigned)ceil_div(nvec, kClThreads), (unsigned)std::min<int64_t>(units, 65535));
+        fwd_channel_last_kernel<T, W, 4>
+            <<<grid, kClThreads, 0, stream>>>(a, strip, nstrips, wvec, bvec);
+        return cudaGetLastError();
+    }
+    const bool rows_dense = a.x_sl == 1 && a.o_sl == 1 && a.x_sd == a.L && a.o_sd == a.L &&
+                            (a.B == 1 || (a.x_sb == a.D * a.L && a.o_sb == a.D * a.L));
+    if (rows_dense && a.L >= 8 && host_aligned16(a.x) && host_aligned16(a.out)) {
+        const int64_t total = a.B * a.D * a.L;
+        const int64_t chunks = ceil_div(total, 256);  // one warp iteration each
+        // Enough warps to fill every SM several times over, each walking a few chunks.
+        const int iters = (int)std::max<int64_t>(1, std::min<int64_t>(8, chunks / (148 * 64)));
+        const int64_t warps = ceil_div(chunks, iters);
+        const int64_t blocks = ceil_div(warps * 32, kCfThreads);
+        fwd_channel_first_kernel<T, W><<<(unsigned)blocks, kCfThreads, 0, stream>>>(a, total, iters);
+        return cudaGetLastError();
+    }
+    const int strip = 64;
+    const int nstrips = (int)ceil_div(a.L, strip);
+    const int64_t n = a.B * a.D * nstrips;
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, kGenThreads), 148 * 64);
+    fwd_generic_kernel<T, W><<<(unsigned)blocks, kGenThreads, 0, stream>>>(a, strip, nstrips);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_fwd(const FwdArgs& a, int width, int dtype, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_fwd<T, kW>(a, stream))));
+    return err;
+}
+
+}  // namespace cc1d

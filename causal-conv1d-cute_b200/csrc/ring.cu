@@ -1,0 +1,143 @@
+// Single-token decode on a ring conv state (replaces ConvUpdateRing, causal_conv1d_cute/ring.py).
+//
+// The ring state (slots, W-1, D) keeps the last W-1 inputs of a sequence unordered: row
+// seen % (W-1) holds the oldest. A step reads the W-1 rows and x, writes the output and
+// overwrites only the oldest row with x, so it stores one state row instead of W-1. Each thread
+// owns a 16-byte vector of channels of one batch row. The rows are already time-major vectors;
+// tap k (oldest first) takes row (pos + k) % (W-1), picked from registers by a select chain so
+// that the weight loads never wait on the sequence length. The taps are summed oldest first, the
+// order of the ordered-state decode, so both layouts give identical outputs.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cc1d {
+
+namespace {
+
+constexpr int kRingThreads = 128;
+constexpr int kGenThreads = 256;
+
+__device__ __forceinline__ int ring_pos(int32_t seen, int K) {
+    int p = seen % K;
+    return p < 0 ? p + K : p;
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    const int64_t nvec = a.D / V;
+    const int64_t j = (int64_t)blockIdx.x * kRingThreads + threadIdx.x;
+    if (j >= nvec) return;
+    const int64_t c0 = j * V;
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = a.silu != 0;
+    for (int64_t b = blockIdx.y; b < a.B; b += gridDim.y) {
+        const uint4 xr = ldg16((const T*)a.x + b * a.x_sb + c0);
+        const int pos = ring_pos(__ldg(a.seen + b), K);
+        const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
+        if (slot == a.pad) continue;
+        if (slot < 0 || (int64_t)slot >= a.nslots) {
+            if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+            continue;
+        }
+        T* rb = (T*)a.ring + (int64_t)slot * a.r_slot + c0;
+        uint4 rows[K];
+#pragma unroll
+        for (int q = 0; q < K; ++q) rows[q] = ld16(rb + q * a.r_sk);
+        float acc[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = bv[e];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            int r = pos + k;
+            r = r >= K ? r - K : r;
+            uint4 v = rows[0];
+#pragma unroll
+            for (int q = 1; q < K; ++q) v = (r == q) ? rows[q] : v;
+            float f[V];
+            unpack16<T>(v, f);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], w[k][e], acc[e]);
+        }
+        {
+            float f[V];
+            unpack16<T>(xr, f);
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                acc[e] = fmaf(f[e], w[K][e], acc[e]);
+                acc[e] = activate<T>(acc[e], use_silu);
+            }
+        }
+        st16(rb + pos * a.r_sk, xr);
+        st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
+    }
+}
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kGenThreads) ring_generic_kernel(const RingArgs a) {
+    constexpr int K = W - 1;
+    const int64_t n = a.B * a.D;
+    const bool use_silu = a.silu != 0;
+    for (int64_t id = (int64_t)blockIdx.x * kGenThreads + threadIdx.x; id < n;
+         id += (int64_t)gridDim.x * kGenThreads) {
+        const int64_t c = id % a.D;
+        const int64_t b = id / a.D;
+        const int32_t slot = a.idx != nullptr ? a.idx[b] : (int32_t)b;
+        if (slot == a.pad) continue;
+        if (slot < 0 || (int64_t)slot >= a.nslots) {
+            if (c == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+            continue;
+        }
+        const int pos = ring_pos(a.seen[b], K);
+        float w[W], bb;
+        load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c, w, bb);
+        T* rb = (T*)a.ring + (int64_t)slot * a.r_slot + c * a.r_sd;
+        const T xv = ((const T*)a.x)[b * a.x_sb + c * a.x_sd];
+        float acc = bb;
+        for (int k = 0; k < K; ++k) {
+            int r = pos + k;
+            r = r >= K ? r - K : r;
+            acc = fmaf(to_f32<T>(rb[r * a.r_sk]), w[k], acc);
+        }
+        acc = fmaf(to_f32<T>(xv), w[K], acc);
+        rb[pos * a.r_sk] = xv;
+        ((T*)a.out)[b * a.o_sb + c * a.o_sd] = from_f32<T>(activate<T>(acc, use_silu));
+    }
+}
+
+template <typename T, int W>
+cudaError_t run_ring(const RingArgs& a, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    const int64_t e = sizeof(T);
+    const bool wvec = a.w_sd == W && a.w_sk == 1 && host_aligned16(a.w);
+    const bool bvec = a.bias != nullptr && a.bias_s == 1 && host_aligned16(a.bias);
+    const bool vec = a.x_sd == 1 && a.o_sd == 1 && a.r_sd == 1 && a.D % V == 0 &&
+                     host_aligned16(a.x) && host_aligned16(a.out) && host_aligned16(a.ring) &&
+                     (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0 &&
+                     (a.r_slot * e) % 16 == 0 && (a.r_sk * e) % 16 == 0;
+    if (vec) {
+        const int64_t nvec = a.D / V;
+        dim3 grid((unsigned)ceil_div(nvec, kRingThreads), (unsigned)std::min<int64_t>(a.B, 65535));
+        ring_kernel<T, W><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
+        return cudaGetLastError();
+    }
+    const int64_t n = a.B * a.D;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, kGenThreads), 148 * 32));
+    ring_generic_kernel<T, W><<<(unsigned)blocks, kGenThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_ring(const RingArgs& a, int width, int dtype, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_ring<T, kW>(a, stream))));
+    return err;
+}
+
+}  // namespace cc1d

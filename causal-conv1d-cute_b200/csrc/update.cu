@@ -1,0 +1,283 @@
+// Decode: one or several tokens per batch row against a conv-state cache updated in place
+// (replaces the decode kernels of causal_conv1d_cute/update.py and ConvUpdateIndexed /
+// ConvUpdateIndexedVec of varlen.py).
+//
+// update_kernel: one thread owns a 16-byte vector of V adjacent channels of one batch row. It
+// issues every load it needs at once (the filter, the x rows, then the slot index and the
+// state block of V*SS contiguous elements), so the only serial dependency is slot -> state.
+// The state block is transposed in registers into SS "time-major" vectors (lane e = channel e),
+// the same shape as an x row, so that stepping the window is a move of whole vectors and the
+// new state, the per-step windows and the outputs are written back as whole 16-byte vectors.
+// State and per-step windows are moved as raw bits: they are bit-exact copies of the inputs.
+//
+// update_generic_kernel: one channel per thread, any strides, any state length >= W-1.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cc1d {
+
+namespace {
+
+constexpr int kUpdThreads = 128;
+constexpr int kGenThreads = 256;
+
+enum { kInterNone = 0, kInterDense = 1, kInterDedup = 2 };
+
+// Transpose between the channel-major state block (element e*SS + s of the block, V*SS
+// elements in SS vectors) and SS time-major vectors (vector s, lane e).
+template <typename T, int SS>
+__device__ __forceinline__ void block_to_time(const uint4 (&blk)[SS], uint4 (&tm)[SS]) {
+    constexpr int V = Vec<T>::V;
+#pragma unroll
+    for (int e = 0; e < V; ++e)
+#pragma unroll
+        for (int s = 0; s < SS; ++s) {
+            const int flat = e * SS + s;
+            set_lane<T>(tm[s], e, lane_of<T>(blk[flat / V], flat % V));
+        }
+}
+
+template <typename T, int N>
+__device__ __forceinline__ void time_to_block(const uint4* tm, uint4 (&blk)[N]) {
+    constexpr int V = Vec<T>::V;
+#pragma unroll
+    for (int q = 0; q < N; ++q)
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const int flat = q * V + i;
+            set_lane<T>(blk[q], i, lane_of<T>(tm[flat % N], flat / N));
+        }
+}
+
+template <typename T, int W, int SS, int LMAX, int IMODE>
+__global__ void __launch_bounds__(kUpdThreads)
+    update_kernel(const UpdArgs a, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    static_assert(SS >= K, "state shorter than the filter history");
+    extern __shared__ uint4 dedup_smem[];
+    const int64_t nvec = a.D / V;
+    const int64_t j = (int64_t)blockIdx.x * kUpdThreads + threadIdx.x;
+    if (j >= nvec) return;
+    const int64_t c0 = j * V;
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = a.silu != 0;
+    for (int64_t b = blockIdx.y; b < a.B; b += gridDim.y) {
+        const T* xb = (const T*)a.x + b * a.x_sb + c0;
+        uint4 xr[LMAX];
+#pragma unroll
+        for (int t = 0; t < LMAX; ++t)
+            if (t < a.L) xr[t] = ldg16(xb + t * a.x_st);
+        const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
+        if (slot == a.pad) continue;
+        if (slot < 0 || (int64_t)slot >= a.nslots) {
+            if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+            continue;
+        }
+        T* sp = (T*)a.state + (int64_t)slot * a.s_slot + c0 * SS;
+        uint4 sr[SS];
+#pragma unroll
+        for (int q = 0; q < SS; ++q) sr[q] = ld16(sp + q * V);
+        T* ib = nullptr;
+        if (IMODE != kInterNone) {
+            const int32_t islot = a.iidx != nullptr ? __ldg(a.iidx + b) : slot;
+            if (islot < 0 || (int64_t)islot >= a.inter_nslots) {
+                if (j == 0) flag_status(a.status, CC1D_DEV_BAD_INTER_SLOT);
+            } else {
+                ib = (T*)a.inter + (int64_t)islot * a.i_slot;
+            }
+        }
+        uint4 win[SS];
+        block_to_time<T, SS>(sr, win);
+        T* ob = (T*)a.out + b * a.o_sb + c0;
+#pragma unroll
+        for (int t = 0; t < LMAX; ++t) {
+            if (t < a.L) {
+                float acc[V];
+#pragma unroll
+                for (int e = 0; e < V; ++e) acc[e] = bv[e];
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    float f[V];
+                    unpack16<T>(win[SS - K + k], f);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], w[k][e], acc[e]);
+                }
+                {
+                    float f[V];
+                    unpack16<T>(xr[t], f);
+#pragma unroll
+                    for (int e = 0; e < V; ++e) {
+                        acc[e] = fmaf(f[e], w[K][e], acc[e]);
+                        acc[e] = activate<T>(acc[e], use_silu);
+                    }
+                }
+                st16(ob + t * a.o_st, pack16<T>(acc));
+#pragma unroll
+                for (int s = 0; s + 1 < SS; ++s) win[s] = win[s + 1];
+                win[SS - 1] = xr[t];
+                if (IMODE == kInterDense && ib != nullptr) {
+                    uint4 blk[K];
+                    time_to_block<T, K>(win + (SS - K), blk);
+                    T* dst = ib + t * a.i_st + c0 * K;
+#pragma unroll
+                    for (int q = 0; q < K; ++q) st16(dst + q * V, blk[q]);
+                }
+            }
+        }
+        {
+            uint4 blk[SS];
+            time_to_block<T, SS>(win, blk);
+#pragma unroll
+            for (int q = 0; q < SS; ++q) st16(sp + q * V, blk[q]);
+        }
+        if (IMODE == kInterDedup && ib != nullptr) {
+            // Row of PW = L + K - 1 elements per channel: the newest K-1 old state entries, then
+            // the L inputs. Staged per thread in shared memory because PW is a runtime value.
+            constexpr int PWMAX = LMAX + K - 1;
+            const int PW = a.L + K - 1;
+            T* reg = reinterpret_cast<T*>(dedup_smem + threadIdx.x * PWMAX);
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+#pragma unroll
+                for (int p = 0; p + 1 < K; ++p) {
+                    const int flat = e * SS + (SS - K + 1 + p);
+                    reg[e * PW + p] = lane_of<T>(sr[flat / V], flat % V);
+                }
+#pragma unroll
+                for (int t = 0; t < LMAX; ++t)
+                    if (t < a.L) reg[e * PW + K - 1 + t] = lane_of<T>(xr[t], e);
+            }
+            const uint4* rv = dedup_smem + threadIdx.x * PWMAX;
+            T* dst = ib + c0 * PW;
+#pragma unroll
+            for (int q = 0; q < PWMAX; ++q)
+                if (q < PW) st16(dst + q * V, rv[q]);
+        }
+    }
+}
+
+// Any strides, any state length S >= W-1 (the whole row shifts by L), any per-step layout.
+template <typename T, int W>
+__global__ void __launch_bounds__(kGenThreads) update_generic_kernel(const UpdArgs a) {
+    constexpr int K = W - 1;
+    const int64_t n = a.B * a.D;
+    const bool use_silu = a.silu != 0;
+    for (int64_t id = (int64_t)blockIdx.x * kGenThreads + threadIdx.x; id < n;
+         id += (int64_t)gridDim.x * kGenThreads) {
+        const int64_t c = id % a.D;
+        const int64_t b = id / a.D;
+        const int32_t slot = a.idx != nullptr ? a.idx[b] : (int32_t)b;
+        if (slot == a.pad) continue;
+        if (slot < 0 || (int64_t)slot >= a.nslots) {
+            if (c == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+            continue;
+        }
+        float w[W], bb;
+        load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c, w, bb);
+        const T* xr = (const T*)a.x + b * a.x_sb + c * a.x_sd;
+        T* st = (T*)a.state + (int64_t)slot * a.s_slot + c * a.s_sd;
+        const int64_t S = a.S;
+        const int L = a.L;
+        // hist = [state row (S) | x (L)]; element m of it:
+        auto hist = [&](int64_t m) -> T { return m < S ? st[m * a.s_sk] : xr[(m - S) * a.x_st]; };
+        T* orow = (T*)a.out + b * a.o_sb + c * a.o_sd;
+        for (int t = 0; t < L; ++t) {
+            float acc = bb;
+#pragma unroll
+            for (int k = 0; k < W; ++k) acc = fmaf(to_f32<T>(hist(S + t - K + k)), w[k], acc);
+            orow[t * a.o_st] = from_f32<T>(activate<T>(acc, use_silu));
+        }
+        if (a.inter != nullptr) {
+            const int32_t islot = a.iidx != nullptr ? a.iidx[b] : slot;
+            if (islot < 0 || (int64_t)islot >= a.inter_nslots) {
+                if (c == 0) flag_status(a.status, CC1D_DEV_BAD_INTER_SLOT);
+            } else {
+                T* ib = (T*)a.inter + (int64_t)islot * a.i_slot + c * a.i_sd;
+                for (int t = 0; t < L; ++t)
+                    for (int k = 0; k < K; ++k) ib[t * a.i_st + k * a.i_sk] = hist(S + t + 1 - K + k);
+            }
+        }
+        // Shift the row left by L in place; ascending order reads every old entry before it is
+        // overwritten.
+        for (int64_t s = 0; s < S; ++s) st[s * a.s_sk] = hist(s + L);
+    }
+}
+
+template <typename T, int W, int SS, int LMAX, int IMODE>
+cudaError_t launch_vec(const UpdArgs& a, bool wvec, bool bvec, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    const int64_t nvec = a.D / V;
+    dim3 grid((unsigned)ceil_div(nvec, kUpdThreads), (unsigned)std::min<int64_t>(a.B, 65535));
+    size_t smem = IMODE == kInterDedup ? (size_t)kUpdThreads * (LMAX + W - 2) * 16 : 0;
+    update_kernel<T, W, SS, LMAX, IMODE><<<grid, kUpdThreads, smem, stream>>>(a, wvec, bvec);
+    return cudaGetLastError();
+}
+
+template <typename T, int W, int SS, int LMAX>
+cudaError_t launch_vec_inter(const UpdArgs& a, int imode, bool wvec, bool bvec,
+                             cudaStream_t stream) {
+    if (imode == kInterDense) return launch_vec<T, W, SS, LMAX, kInterDense>(a, wvec, bvec, stream);
+    if (imode == kInterDedup) return launch_vec<T, W, SS, LMAX, kInterDedup>(a, wvec, bvec, stream);
+    return launch_vec<T, W, SS, LMAX, kInterNone>(a, wvec, bvec, stream);
+}
+
+template <typename T, int W>
+cudaError_t run_update(const UpdArgs& a, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    constexpr int P = W <= 2 ? 2 : W <= 4 ? 4 : 8;  // power of two >= W (padded layout)
+    const int64_t e = sizeof(T);
+    const bool wvec = a.w_sd == W && a.w_sk == 1 && host_aligned16(a.w);
+    const bool bvec = a.bias != nullptr && a.bias_s == 1 && host_aligned16(a.bias);
+    const bool xok = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
+                     host_aligned16(a.out) && (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0 &&
+                     (a.L == 1 || ((a.x_st * e) % 16 == 0 && (a.o_st * e) % 16 == 0));
+    const bool sok = a.s_sk == 1 && a.s_sd == a.S && host_aligned16(a.state) &&
+                     (a.s_slot * e) % 16 == 0;
+    int imode = kInterNone;
+    bool iok = true;
+    if (a.inter != nullptr) {
+        const int64_t PW = a.L + K - 1;
+        iok = host_aligned16(a.inter) && (a.i_slot * e) % 16 == 0 && a.S == K;
+        if (a.i_sk == 1 && a.i_sd == K && a.i_st == a.D * K) {
+            imode = kInterDense;
+        } else if (a.i_sk == 1 && a.i_sd == PW && a.i_st == 1) {
+            imode = kInterDedup;
+        } else {
+            iok = false;
+        }
+    }
+    if (xok && sok && iok && a.L >= 1 && a.L <= 16) {
+        if (a.S == K) {
+            if (a.L == 1) {
+                // A single step: dense and dedup per-step layouts coincide.
+                return launch_vec_inter<T, W, K, 1>(a, imode == kInterNone ? kInterNone : kInterDense,
+                                                    wvec, bvec, stream);
+            }
+            if (a.L <= 4) return launch_vec_inter<T, W, K, 4>(a, imode, wvec, bvec, stream);
+            if (a.L <= 8) return launch_vec_inter<T, W, K, 8>(a, imode, wvec, bvec, stream);
+            return launch_vec_inter<T, W, K, 16>(a, imode, wvec, bvec, stream);
+        }
+        if (a.S == P && P != K && a.L == 1 && imode == kInterNone)
+            return launch_vec<T, W, P, 1, kInterNone>(a, wvec, bvec, stream);
+    }
+    const int64_t n = a.B * a.D;
+    const int64_t blocks = std::min<int64_t>(ceil_div(n, kGenThreads), 148 * 32);
+    update_generic_kernel<T, W><<<(unsigned)std::max<int64_t>(blocks, 1), kGenThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_update(const UpdArgs& a, int width, int dtype, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_update<T, kW>(a, stream))));
+    return err;
+}
+
+}  // namespace cc1d

@@ -1,0 +1,367 @@
+// Packed variable-length prefill in one launch (replaces the strip walk + ConvSeqBoundary /
+// ConvSeqBoundaryVec pair of causal_conv1d_cute/varlen.py, which needs two launches for more
+// than one sequence).
+//
+// The packed stream of T tokens is cut into strips of S tokens; a thread owns one strip of one
+// channel group. Sequence bounds come from query_start_loc on the device (binary search for the
+// strip start, then a walk), so the call needs no host synchronisation.
+//
+// Ownership. The first W-1 outputs of a sequence depend on its initial state, and its final
+// state is written into the same cache slot. Both belong to the thread whose strip holds the
+// sequence's first token (its "owner"): it reads the initial state, computes the head outputs
+// (running past its strip end when the sequence starts in the last W-2 tokens of the strip),
+// then writes the final state. Every other strip of the sequence starts W-1 tokens after the
+// sequence start at the earliest and reads only the sequence's own inputs. No slot is read by one
+// thread and written by another, so one launch suffices.
+//
+// The final state is the last W-1 inputs of [initial state | sequence]; it is copied as raw bits
+// from x (or from the initial state when the sequence is shorter than W-1 tokens).
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace cc1d {
+
+namespace {
+
+constexpr int kVarThreads = 128;
+constexpr int kGenThreads = 256;
+
+// query_start_loc[s] clamped into [0, T].
+__device__ __forceinline__ int64_t qsl_at(const VarArgs& a, int64_t s) {
+    const int64_t v = __ldg(a.qsl + s);
+    return v < 0 ? 0 : (v > a.T ? a.T : v);
+}
+
+// Largest s in [0, nseq] with query_start_loc[s] <= t, or -1 when t precedes the first sequence.
+// Empty sequences are skipped because the largest index wins.
+__device__ int64_t seq_of(const VarArgs& a, int64_t t) {
+    if (qsl_at(a, 0) > t) return -1;
+    int64_t lo = 0, hi = a.nseq;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (qsl_at(a, mid) <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ void check_bounds(const VarArgs& a, int64_t s) {
+    const int32_t lo = __ldg(a.qsl + s), hi = __ldg(a.qsl + s + 1);
+    if (lo < 0 || hi > a.T || hi < lo) flag_status(a.status, CC1D_DEV_BAD_QSL);
+}
+
+struct SeqSlot {
+    bool live;      // the cache slot is read and written
+    bool use_init;  // the sequence starts from the cached state
+    int64_t slot;
+};
+
+__device__ __forceinline__ SeqSlot seq_slot(const VarArgs& a, int64_t s, bool report) {
+    SeqSlot r{false, false, 0};
+    if (a.states == nullptr) return r;
+    const int32_t slot = a.cidx != nullptr ? __ldg(a.cidx + s) : (int32_t)s;
+    if (slot == a.pad) return r;
+    if (slot < 0 || (int64_t)slot >= a.nslots) {
+        if (report) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+        return r;
+    }
+    r.live = true;
+    r.slot = slot;
+    r.use_init = a.hinit != nullptr && __ldg(a.hinit + s) != 0;
+    return r;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Token-major: x rows of D adjacent channels, x_st elements apart
+// ---------------------------------------------------------------------------------------------
+
+template <typename T, int W, int U>
+__device__ __forceinline__ void walk_rows(const T* xb, int64_t x_st, T* ob, int64_t o_st,
+                                          int64_t ta, int64_t tb, float (&h)[W - 1][Vec<T>::V],
+                                          const float (&w)[W][Vec<T>::V],
+                                          const float (&bv)[Vec<T>::V], bool use_silu) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    int64_t t = ta;
+    for (; t + U <= tb; t += U) {
+        uint4 r[U];
+#pragma unroll
+        for (int i = 0; i < U; ++i) r[i] = ldg16_stream(xb + (t + i) * x_st);
+#pragma unroll
+        for (int i = 0; i < U; ++i) {
+            float xv[V], o[V];
+            unpack16<T>(r[i], xv);
+#pragma unroll
+            for (int e = 0; e < V; ++e) {
+                float acc = bv[e];
+#pragma unroll
+                for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
+                acc = fmaf(xv[e], w[K][e], acc);
+                o[e] = activate<T>(acc, use_silu);
+            }
+#pragma unroll
+            for (int k = 0; k + 1 < K; ++k)
+#pragma unroll
+                for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
+#pragma unroll
+            for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
+            st16_stream(ob + (t + i) * o_st, pack16<T>(o));
+        }
+    }
+    for (; t < tb; ++t) {
+        float xv[V], o[V];
+        unpack16<T>(ldg16_stream(xb + t * x_st), xv);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+            float acc = bv[e];
+#pragma unroll
+            for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
+            acc = fmaf(xv[e], w[K][e], acc);
+            o[e] = activate<T>(acc, use_silu);
+        }
+#pragma unroll
+        for (int k = 0; k + 1 < K; ++k)
+#pragma unroll
+            for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
+#pragma unroll
+        for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
+        st16_stream(ob + t * o_st, pack16<T>(o));
+    }
+}
+
+template <typename T, int W, int U>
+__global__ void __launch_bounds__(kVarThreads)
+    varlen_token_major_kernel(const VarArgs a, int strip, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    const int64_t nvec = a.D / V;
+    const int64_t j = (int64_t)blockIdx.x * kVarThreads + threadIdx.x;
+    if (j >= nvec) return;
+    const int64_t c0 = j * V;
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = a.silu != 0;
+    const T* xb = (const T*)a.x + c0;
+    T* ob = (T*)a.out + c0;
+    const int64_t nstrips = ceil_div(a.T, strip);
+    for (int64_t u = blockIdx.y; u < nstrips; u += gridDim.y) {
+        const int64_t t0 = u * strip;
+        const int64_t t1 = min(t0 + strip, a.T);
+        int64_t s = seq_of(a, t0);
+        int64_t t = t0;
+        if (s < 0) {
+            t = min(t1, qsl_at(a, 0));
+            s = 0;
+        }
+        while (t < t1 && s < a.nseq) {
+            const int64_t bos = qsl_at(a, s);
+            const int64_t eos = max(qsl_at(a, s + 1), bos);
+            if (eos <= t) {
+                ++s;
+                continue;
+            }
+            const int64_t e = min(t1, eos);
+            float h[K][V];
+            if (t == bos) {
+                // Owner of sequence s.
+                if (j == 0) check_bounds(a, s);
+                const SeqSlot ss = seq_slot(a, s, j == 0);
+                T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c0 * K : nullptr;
+                uint4 init[K];
+                if (ss.use_init) {
+                    uint4 blk[K];
+#pragma unroll
+                    for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
+#pragma unroll
+                    for (int ee = 0; ee < V; ++ee)
+#pragma unroll
+                        for (int k = 0; k < K; ++k) {
+                            const int flat = ee * K + k;
+                            set_lane<T>(init[k], ee, lane_of<T>(blk[flat / V], flat % V));
+                        }
+                } else {
+#pragma unroll
+                    for (int k = 0; k < K; ++k) init[k] = make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int k = 0; k < K; ++k) unpack16<T>(init[k], h[k]);
+                const int64_t end = min(eos, max(e, bos + K));
+                walk_rows<T, W, U>(xb, a.x_st, ob, a.o_st, bos, end, h, w, bv, use_silu);
+                if (ss.live) {
+                    const int64_t n = eos - bos;
+                    uint4 fin[K];
+#pragma unroll
+                    for (int k = 0; k < K; ++k) {
+                        const int64_t pos = eos - K + k;
+                        if (pos >= bos) {
+                            fin[k] = ldg16(xb + pos * a.x_st);
+                        } else {
+                            // n < K: entry k + n of the initial state.
+                            const int64_t m = k + n;
+                            uint4 v = init[0];
+#pragma unroll
+                            for (int q = 1; q < K; ++q) v = (m == q) ? init[q] : v;
+                            fin[k] = v;
+                        }
+                    }
+                    uint4 blk[K];
+#pragma unroll
+                    for (int q = 0; q < K; ++q)
+#pragma unroll
+                        for (int i = 0; i < V; ++i) {
+                            const int flat = q * V + i;
+                            set_lane<T>(blk[q], i, lane_of<T>(fin[flat % K], flat / K));
+                        }
+#pragma unroll
+                    for (int q = 0; q < K; ++q) st16(sp + q * V, blk[q]);
+                }
+            } else {
+                const int64_t start = max(t, bos + K);
+                if (start < e) {
+#pragma unroll
+                    for (int k = 0; k < K; ++k)
+                        unpack16<T>(ldg16(xb + (start - K + k) * a.x_st), h[k]);
+                    walk_rows<T, W, U>(xb, a.x_st, ob, a.o_st, start, e, h, w, bv, use_silu);
+                }
+            }
+            t = e;
+            if (e == eos) ++s;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Any strides: one channel per thread, same ownership rules.
+// ---------------------------------------------------------------------------------------------
+
+template <typename T, int W>
+__global__ void __launch_bounds__(kGenThreads) varlen_generic_kernel(const VarArgs a, int strip) {
+    constexpr int K = W - 1;
+    const int64_t nstrips = ceil_div(a.T, strip);
+    const int64_t n = nstrips * a.D;
+    const bool use_silu = a.silu != 0;
+    const T* x = (const T*)a.x;
+    T* out = (T*)a.out;
+    for (int64_t id = (int64_t)blockIdx.x * kGenThreads + threadIdx.x; id < n;
+         id += (int64_t)gridDim.x * kGenThreads) {
+        const int64_t c = id % a.D;
+        const int64_t u = id / a.D;
+        float w[W], bb;
+        load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c, w, bb);
+        const T* xr = x + c * a.x_sd;
+        T* orow = out + c * a.o_sd;
+        auto walk = [&](int64_t ta, int64_t tb, float (&h)[K]) {
+            for (int64_t t = ta; t < tb; ++t) {
+                const float xv = to_f32<T>(xr[t * a.x_st]);
+                float acc = bb;
+#pragma unroll
+                for (int k = 0; k < K; ++k) acc = fmaf(h[k], w[k], acc);
+                acc = fmaf(xv, w[K], acc);
+                orow[t * a.o_st] = from_f32<T>(activate<T>(acc, use_silu));
+#pragma unroll
+                for (int k = 0; k + 1 < K; ++k) h[k] = h[k + 1];
+                h[K - 1] = xv;
+            }
+        };
+        const int64_t t0 = u * strip;
+        const int64_t t1 = min(t0 + strip, a.T);
+        int64_t s = seq_of(a, t0);
+        int64_t t = t0;
+        if (s < 0) {
+            t = min(t1, qsl_at(a, 0));
+            s = 0;
+        }
+        while (t < t1 && s < a.nseq) {
+            const int64_t bos = qsl_at(a, s);
+            const int64_t eos = max(qsl_at(a, s + 1), bos);
+            if (eos <= t) {
+                ++s;
+                continue;
+            }
+            const int64_t e = min(t1, eos);
+            float h[K];
+            if (t == bos) {
+                if (c == 0) check_bounds(a, s);
+                const SeqSlot ss = seq_slot(a, s, c == 0);
+                T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c * a.s_sd : nullptr;
+                T init[K];
+#pragma unroll
+                for (int k = 0; k < K; ++k) {
+                    init[k] = ss.use_init ? sp[k * a.s_sk] : from_f32<T>(0.f);
+                    h[k] = to_f32<T>(init[k]);
+                }
+                walk(bos, min(eos, max(e, bos + K)), h);
+                if (ss.live) {
+                    const int64_t nn = eos - bos;
+#pragma unroll
+                    for (int k = 0; k < K; ++k) {
+                        const int64_t pos = eos - K + k;
+                        T v;
+                        if (pos >= bos) {
+                            v = xr[pos * a.x_st];
+                        } else {
+                            const int64_t m = k + nn;
+                            v = init[0];
+#pragma unroll
+                            for (int q = 1; q < K; ++q) v = (m == q) ? init[q] : v;
+                        }
+                        sp[k * a.s_sk] = v;
+                    }
+                }
+            } else {
+                const int64_t start = max(t, bos + K);
+                if (start < e) {
+#pragma unroll
+                    for (int k = 0; k < K; ++k) h[k] = to_f32<T>(xr[(start - K + k) * a.x_st]);
+                    walk(start, e, h);
+                }
+            }
+            t = e;
+            if (e == eos) ++s;
+        }
+    }
+}
+
+// Strip length of the token-major walk: 64 tokens keeps the halo re-read under 5% at W = 4 while
+// leaving ~1e6 threads at the serving shapes.
+int varlen_strip(int64_t T) { return T <= 64 ? (int)std::max<int64_t>(T, 1) : 64; }
+
+template <typename T, int W>
+cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    const int64_t e = sizeof(T);
+    const bool wvec = a.w_sd == W && a.w_sk == 1 && host_aligned16(a.w);
+    const bool bvec = a.bias != nullptr && a.bias_s == 1 && host_aligned16(a.bias);
+    const bool sok = a.states == nullptr ||
+                     (a.s_sk == 1 && a.s_sd == K && host_aligned16(a.states) &&
+                      (a.s_slot * e) % 16 == 0);
+    const bool tm = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
+                    host_aligned16(a.out) && (a.x_st * e) % 16 == 0 && (a.o_st * e) % 16 == 0;
+    if (tm && sok) {
+        const int strip = varlen_strip(a.T);
+        const int64_t nstrips = ceil_div(a.T, strip);
+        const int64_t nvec = a.D / V;
+        dim3 grid((unsigned)ceil_div(nvec, kVarThreads), (unsigned)std::min<int64_t>(nstrips, 65535));
+        varlen_token_major_kernel<T, W, 4><<<grid, kVarThreads, 0, stream>>>(a, strip, wvec, bvec);
+        return cudaGetLastError();
+    }
+    const int strip = 64;
+    const int64_t n = ceil_div(a.T, strip) * a.D;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, kGenThreads), 148 * 32));
+    varlen_generic_kernel<T, W><<<(unsigned)blocks, kGenThreads, 0, stream>>>(a, strip);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_varlen(const VarArgs& a, int width, int dtype, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_varlen<T, kW>(a, stream))));
+    return err;
+}
+
+}  // namespace cc1d
