@@ -17,8 +17,9 @@ all-gather a sample of every rank's outputs and compare them bit for bit with th
 
 With N = 1 the other BASELINE paths are measured too ("paths"): indexed decode (config 3) and its
 ring variant, the 4-step speculative verify with dense per-step states (config 4), and packed
-varlen prefill (config 5) at widths 2, 3, 4 and 8. Decode inputs fit in L2, so every timed decode
-call is preceded by a write of 256 MiB (cold L2), and the warm figure is reported beside it.
+varlen prefill (config 5) at widths 2, 3, 4 and 8, each replayed in a CUDA graph (no host
+launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
+exceeds L2, and "warm" repeats one set.
 
 --impl reference times the reference's CPU algorithm (the C port of its PyTorch fallback,
 oracle/cc1d_oracle.c) on the host cores, on bounded samples of the same workload.
@@ -185,16 +186,6 @@ def time_launches(step, steps, flush=None):
     return starts[0].elapsed_time(ends[-1]), per
 
 
-_flush_buf = None
-
-
-def flush_l2():
-    global _flush_buf
-    if _flush_buf is None:
-        _flush_buf = torch.empty(256 * 2**20, dtype=torch.uint8, device="cuda")
-    _flush_buf.fill_(1)
-
-
 # ---------------------------------------------------------------------------------------------
 # Headline: prefill config 2
 # ---------------------------------------------------------------------------------------------
@@ -287,12 +278,42 @@ def run_headline(args, rank, world, device):
 # ---------------------------------------------------------------------------------------------
 
 
-def _stats(per_ms):
-    per = sorted(per_ms)
-    return statistics.median(per) * 1e3
+def _median_us(per_ms):
+    return statistics.median(per_ms) * 1e3
 
 
-def run_paths(device, reps=200):
+def graph_us(calls, reps):
+    """Microseconds per call of `calls` (one callable per input set) replayed in a CUDA graph.
+
+    All calls are captured once, back to back, and the graph is replayed `reps` times between two
+    events, so host launch overhead is excluded and every call follows the previous one as it
+    would inside a captured serving step.
+    """
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for f in calls:
+            f()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in calls:
+            f()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / (reps * len(calls))
+
+
+def run_paths(device, reps=50, sets=8):
+    """Decode paths: `sets` independent input sets (together larger than L2) are cycled, so each
+    call reads cold data ("cold"); "warm" repeats one set. Varlen inputs exceed L2 by themselves."""
     import causal_conv1d_cute as C
 
     g = torch.Generator(device=device).manual_seed(7)
@@ -301,46 +322,45 @@ def run_paths(device, reps=200):
     w4 = (torch.rand(D, 4, device=device, generator=g) - 0.5).to(bf)
     bias = (torch.randn(D, device=device, generator=g) * 0.1).to(bf)
 
-    # Config 3: single-token indexed decode, B=256, 1024-slot cache.
+    def record(name, calls, nbytes, extra=None):
+        cold = graph_us(calls, reps)
+        warm = graph_us(calls[:1] * len(calls), reps)
+        res[name] = {"us_cold": cold, "us_warm": warm, "bytes": nbytes,
+                     "gbs_cold": nbytes / (cold * 1e3), **(extra or {})}
+
+    # Config 3: single-token indexed decode, B=256, 1024-slot cache (48 MiB per set).
     Bd, slots = 256, 1024
-    x = torch.randn(Bd, D, device=device, generator=g).to(bf)
-    cache = torch.randn(slots, D, 3, device=device, generator=g).to(bf)
-    idx = torch.randperm(slots, device=device, generator=g)[:Bd].to(torch.int32)
-    nbytes = 4 * Bd * D * 2 + 2 * Bd * D * 3 * 2 + D * 4 * 2 + D * 2 + Bd * 4
-    f = lambda: C.causal_conv1d_update(x, cache, w4, bias, "silu", idx)  # noqa: E731
-    for _ in range(10):
-        f()
-    _, cold = time_launches(f, reps, flush=flush_l2)
-    _, warm = time_launches(f, reps)
-    res["decode_indexed_b256"] = {"us_cold": _stats(cold), "us_warm": _stats(warm),
-                                  "bytes": nbytes, "gbs_cold": nbytes / (_stats(cold) * 1e3)}
+    calls = []
+    for _ in range(sets):
+        x = torch.randn(Bd, D, device=device, generator=g).to(bf)
+        cache = torch.randn(slots, D, 3, device=device, generator=g).to(bf)
+        idx = torch.randperm(slots, device=device, generator=g)[:Bd].to(torch.int32)
+        calls.append(lambda x=x, cache=cache, idx=idx: C.causal_conv1d_update(x, cache, w4, bias, "silu", idx))
+    nbytes = 2 * Bd * D * 2 + 2 * Bd * D * 3 * 2 + D * 4 * 2 + D * 2 + Bd * 4
+    record("decode_indexed_b256", calls, nbytes)
 
     # Config 3 ring variant: ring (256, 3, 8192), seen ~U[1, 8192].
-    ring = torch.randn(Bd, 3, D, device=device, generator=g).to(bf)
-    seen = torch.randint(1, 8193, (Bd,), device=device, generator=g, dtype=torch.int32)
+    calls = []
+    for _ in range(sets):
+        x = torch.randn(Bd, D, device=device, generator=g).to(bf)
+        ring = torch.randn(Bd, 3, D, device=device, generator=g).to(bf)
+        seen = torch.randint(1, 8193, (Bd,), device=device, generator=g, dtype=torch.int32)
+        calls.append(lambda x=x, ring=ring, seen=seen: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen))
     nbytes = 2 * Bd * D * 2 + 3 * Bd * D * 2 + Bd * D * 2 + D * 4 * 2 + D * 2 + Bd * 4
-    f = lambda: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen)  # noqa: E731
-    for _ in range(10):
-        f()
-    _, cold = time_launches(f, reps, flush=flush_l2)
-    _, warm = time_launches(f, reps)
-    res["decode_ring_b256"] = {"us_cold": _stats(cold), "us_warm": _stats(warm), "bytes": nbytes,
-                               "gbs_cold": nbytes / (_stats(cold) * 1e3)}
+    record("decode_ring_b256", calls, nbytes)
 
     # Config 4: spec-decode verify, B=64, 4 steps, dense per-step states.
     Bs, S = 64, 4
-    xs = torch.randn(Bs, S, D, device=device, generator=g).to(bf).transpose(1, 2)
-    st = torch.randn(Bs, D, 3, device=device, generator=g).to(bf)
-    inter = torch.empty(Bs, S, D, 3, device=device, dtype=bf)
-    perm = torch.randperm(Bs, device=device, generator=g).to(torch.int32)
+    calls = []
+    for _ in range(sets):
+        xs = torch.randn(Bs, S, D, device=device, generator=g).to(bf).transpose(1, 2)
+        st = torch.randn(Bs, D, 3, device=device, generator=g).to(bf)
+        inter = torch.empty(Bs, S, D, 3, device=device, dtype=bf)
+        perm = torch.randperm(Bs, device=device, generator=g).to(torch.int32)
+        calls.append(lambda xs=xs, st=st, inter=inter, perm=perm:
+                     C.causal_conv1d_update(xs, st, w4, bias, "silu", perm, -1, inter, perm))
     nbytes = 2 * Bs * S * D * 2 + 2 * Bs * D * 3 * 2 + Bs * S * D * 3 * 2 + D * 4 * 2 + D * 2 + 2 * Bs * 4
-    f = lambda: C.causal_conv1d_update(xs, st, w4, bias, "silu", perm, -1, inter, perm)  # noqa: E731
-    for _ in range(10):
-        f()
-    _, cold = time_launches(f, reps, flush=flush_l2)
-    _, warm = time_launches(f, reps)
-    res["spec_decode_b64_s4"] = {"us_cold": _stats(cold), "us_warm": _stats(warm), "bytes": nbytes,
-                                 "gbs_cold": nbytes / (_stats(cold) * 1e3)}
+    record("spec_decode_b64_s4", calls, nbytes)
 
     # Config 5: varlen, 32 lognormal(7, 1) lengths clipped to [1, 8192], token-major x.
     rng = np.random.default_rng(0)
@@ -355,11 +375,8 @@ def run_paths(device, reps=200):
         states = torch.randn(512, D, Wv - 1, device=device, generator=g).to(bf)
         nh = int(hinit.sum())
         nbytes = 2 * D * T * 2 + D * (Wv - 1) * 2 * (32 + nh) + 4 * 33 + 4 * 32 + 32 + D * Wv * 2
-        f = lambda: C.causal_conv1d_varlen_fn(xv.t(), wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
-        for _ in range(5):
-            f()
-        _, per = time_launches(f, 50)
-        us = _stats(per)
+        f = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xv.t(), wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
+        us = graph_us([f], 20)
         res[f"varlen_w{Wv}"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3), "tokens": T}
     return res
 

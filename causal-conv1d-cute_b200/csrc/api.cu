@@ -37,11 +37,17 @@ cc1d_status_t check_common(int32_t width, int32_t dtype) {
 }
 
 // Make the stream's device current on this thread, so a launch from any host thread lands on
-// the device that owns the stream (the legacy default stream keeps the current device).
+// the device that owns the stream (the legacy default stream keeps the current device). While the
+// stream is being captured into a CUDA graph the device query is not permitted, and the capturing
+// thread already works on the stream's device, so nothing is changed then.
 cc1d_status_t bind_stream(void* stream) {
     if (stream == nullptr) return CC1D_OK;
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    cudaError_t err = cudaStreamIsCapturing((cudaStream_t)stream, &capture);
+    if (err != cudaSuccess) return from_cuda(err, "cudaStreamIsCapturing");
+    if (capture != cudaStreamCaptureStatusNone) return CC1D_OK;
     int dev = -1, cur = -1;
-    cudaError_t err = cudaStreamGetDevice((cudaStream_t)stream, &dev);
+    err = cudaStreamGetDevice((cudaStream_t)stream, &dev);
     if (err != cudaSuccess) return from_cuda(err, "cudaStreamGetDevice");
     err = cudaGetDevice(&cur);
     if (err != cudaSuccess) return from_cuda(err, "cudaGetDevice");

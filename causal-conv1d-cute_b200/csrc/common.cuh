@@ -238,6 +238,42 @@ __device__ __forceinline__ void load_filter(const T* __restrict__ weight, int64_
     }
 }
 
+// The same filter kept as raw storage-type vectors (W tap-major vectors wt[k], lane e = channel
+// c0 + e, plus the bias vector): a quarter of the registers of the fp32 form for bf16/fp16. Decode
+// kernels use each weight once per row, so widening at use costs nothing extra.
+template <typename T, int W>
+__device__ __forceinline__ void load_filter_raw(const T* __restrict__ weight, int64_t w_sd,
+                                                int64_t w_sk, const T* __restrict__ bias,
+                                                int64_t bias_s, int64_t c0, bool wvec, bool bvec,
+                                                uint4 (&wt)[W], uint4& bt) {
+    constexpr int V = Vec<T>::V;
+    if (wvec) {
+        uint4 blk[W];
+#pragma unroll
+        for (int q = 0; q < W; ++q) blk[q] = ldg16(weight + c0 * W + q * V);
+#pragma unroll
+        for (int e = 0; e < V; ++e)
+#pragma unroll
+            for (int k = 0; k < W; ++k) {
+                const int flat = e * W + k;
+                set_lane<T>(wt[k], e, lane_of<T>(blk[flat / V], flat % V));
+            }
+    } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e)
+#pragma unroll
+            for (int k = 0; k < W; ++k) set_lane<T>(wt[k], e, __ldg(weight + (c0 + e) * w_sd + k * w_sk));
+    }
+    if (bias == nullptr) {
+        bt = make_uint4(0, 0, 0, 0);
+    } else if (bvec) {
+        bt = ldg16(bias + c0);
+    } else {
+#pragma unroll
+        for (int e = 0; e < V; ++e) set_lane<T>(bt, e, __ldg(bias + (c0 + e) * bias_s));
+    }
+}
+
 // Weights of one channel, for the scalar kernels.
 template <typename T, int W>
 __device__ __forceinline__ void load_filter1(const T* __restrict__ weight, int64_t w_sd,

@@ -13,47 +13,22 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "walk.cuh"
 
 namespace cc1d {
 
 namespace {
 
-constexpr int kClThreads = 128;
+constexpr int kClThreads = 64;
 constexpr int kCfThreads = 256;
 constexpr int kGenThreads = 256;
 
-// One output vector from the fp32 window h (oldest first) and the new input xv; shifts xv into
-// the window afterwards.
-template <typename T, int W>
-__device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const float* xv,
-                                          const float (&w)[W][Vec<T>::V],
-                                          const float (&bv)[Vec<T>::V], bool use_silu,
-                                          float* o) {
-    constexpr int V = Vec<T>::V;
-    constexpr int K = W - 1;
-#pragma unroll
-    for (int e = 0; e < V; ++e) {
-        float acc = bv[e];
-#pragma unroll
-        for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
-        acc = fmaf(xv[e], w[K][e], acc);
-        o[e] = activate<T>(acc, use_silu);
-    }
-#pragma unroll
-    for (int k = 0; k + 1 < K; ++k)
-#pragma unroll
-        for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
-#pragma unroll
-    for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
-}
-
-template <typename T, int W, int U>
-__global__ void __launch_bounds__(kClThreads)
+template <typename T, int W, int U, bool PF, int NT>
+__global__ void __launch_bounds__(NT)
     fwd_channel_last_kernel(const FwdArgs a, int strip, int nstrips, bool wvec, bool bvec) {
     constexpr int V = Vec<T>::V;
-    constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
-    const int64_t j = (int64_t)blockIdx.x * kClThreads + threadIdx.x;
+    const int64_t j = (int64_t)blockIdx.x * NT + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
     float w[W][V], bv[V];
@@ -67,36 +42,9 @@ __global__ void __launch_bounds__(kClThreads)
         const int64_t t1 = min(t0 + strip, a.L);
         const T* xb = (const T*)a.x + b * a.x_sb + c0;
         T* ob = (T*)a.out + b * a.o_sb + c0;
-        float h[K][V];
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const int64_t t = t0 - K + k;
-            if (t >= 0) {
-                unpack16<T>(ldg16(xb + t * a.x_sl), h[k]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < V; ++e) h[k][e] = 0.f;
-            }
-        }
-        int64_t t = t0;
-        for (; t + U <= t1; t += U) {
-            uint4 r[U];
-#pragma unroll
-            for (int i = 0; i < U; ++i) r[i] = ldg16_stream(xb + (t + i) * a.x_sl);
-#pragma unroll
-            for (int i = 0; i < U; ++i) {
-                float xv[V], o[V];
-                unpack16<T>(r[i], xv);
-                conv_step<T, W>(h, xv, w, bv, use_silu, o);
-                st16_stream(ob + (t + i) * a.o_sl, pack16<T>(o));
-            }
-        }
-        for (; t < t1; ++t) {
-            float xv[V], o[V];
-            unpack16<T>(ldg16_stream(xb + t * a.x_sl), xv);
-            conv_step<T, W>(h, xv, w, bv, use_silu, o);
-            st16_stream(ob + t * a.o_sl, pack16<T>(o));
-        }
+        float h[W - 1][V];
+        load_halo<T, W>(xb, a.x_sl, t0, h);
+        walk_strip<T, W, U, PF>(xb, a.x_sl, ob, a.o_sl, t0, t1, h, w, bv, use_silu);
     }
 }
 
@@ -247,13 +195,14 @@ __global__ void __launch_bounds__(kGenThreads)
 }
 
 // Launch table for the channel-last strip walk: tokens per strip. Short strips give more
-// threads (latency hiding), long strips re-read fewer halo rows; 32 balances the two at the
-// Mamba-2 prefill shapes and is swept by the benchmark.
+// threads (latency hiding), long strips re-read fewer halo rows. Measured on B200 at
+// B=8, L=4096, D=8192 (8 rows in flight per thread, 64-thread CTAs): strips of 16 / 32 / 64 /
+// 128 / 256 tokens ran at 245 / 200 / 185 / 182 / 203 us. Short sequences use one strip.
 int cl_strip(int64_t B, int64_t L, int64_t nvec) {
     (void)B;
     (void)nvec;
-    if (L <= 32) return (int)L;
-    return 32;
+    if (L <= 128) return (int)std::max<int64_t>(L, 1);
+    return 128;
 }
 
 template <typename T, int W>
@@ -271,7 +220,7 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
         const int nstrips = (int)ceil_div(a.L, strip);
         const int64_t units = (int64_t)nstrips * a.B;
         dim3 grid((unsigned)ceil_div(nvec, kClThreads), (unsigned)std::min<int64_t>(units, 65535));
-        fwd_channel_last_kernel<T, W, 4>
+        fwd_channel_last_kernel<T, W, 8, true, kClThreads>
             <<<grid, kClThreads, 0, stream>>>(a, strip, nstrips, wvec, bvec);
         return cudaGetLastError();
     }

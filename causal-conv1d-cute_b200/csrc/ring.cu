@@ -32,50 +32,48 @@ __global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bo
     const int64_t j = (int64_t)blockIdx.x * kRingThreads + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
-    float w[W][V], bv[V];
-    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
-                      w, bv);
-    const bool use_silu = a.silu != 0;
-    for (int64_t b = blockIdx.y; b < a.B; b += gridDim.y) {
-        const uint4 xr = ldg16((const T*)a.x + b * a.x_sb + c0);
-        const int pos = ring_pos(__ldg(a.seen + b), K);
-        const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
-        if (slot == a.pad) continue;
-        if (slot < 0 || (int64_t)slot >= a.nslots) {
-            if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
-            continue;
-        }
-        T* rb = (T*)a.ring + (int64_t)slot * a.r_slot + c0;
-        uint4 rows[K];
-#pragma unroll
-        for (int q = 0; q < K; ++q) rows[q] = ld16(rb + q * a.r_sk);
-        float acc[V];
-#pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = bv[e];
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            int r = pos + k;
-            r = r >= K ? r - K : r;
-            uint4 v = rows[0];
-#pragma unroll
-            for (int q = 1; q < K; ++q) v = (r == q) ? rows[q] : v;
-            float f[V];
-            unpack16<T>(v, f);
-#pragma unroll
-            for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], w[k][e], acc[e]);
-        }
-        {
-            float f[V];
-            unpack16<T>(xr, f);
-#pragma unroll
-            for (int e = 0; e < V; ++e) {
-                acc[e] = fmaf(f[e], w[K][e], acc[e]);
-                acc[e] = activate<T>(acc[e], use_silu);
-            }
-        }
-        st16(rb + pos * a.r_sk, xr);
-        st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
+    // One row per thread (gridDim.y == B) and raw weights widened at use: a lean thread keeps
+    // twice as many of them resident.
+    const int64_t b = blockIdx.y;
+    uint4 wt[W], bt;
+    load_filter_raw<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
+                          bvec, wt, bt);
+    const uint4 xr = ldg16((const T*)a.x + b * a.x_sb + c0);
+    const int pos = ring_pos(__ldg(a.seen + b), K);
+    const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
+    if (slot == a.pad) return;
+    if (slot < 0 || (int64_t)slot >= a.nslots) {
+        if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+        return;
     }
+    T* rb = (T*)a.ring + (int64_t)slot * a.r_slot + c0;
+    uint4 rows[K];
+#pragma unroll
+    for (int q = 0; q < K; ++q) rows[q] = ld16(rb + q * a.r_sk);
+    float acc[V];
+    unpack16<T>(bt, acc);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        int r = pos + k;
+        r = r >= K ? r - K : r;
+        uint4 v = rows[0];
+#pragma unroll
+        for (int q = 1; q < K; ++q) v = (r == q) ? rows[q] : v;
+        float f[V], wk[V];
+        unpack16<T>(v, f);
+        unpack16<T>(wt[k], wk);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
+    }
+    {
+        float f[V], wk[V];
+        unpack16<T>(xr, f);
+        unpack16<T>(wt[K], wk);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), a.silu != 0);
+    }
+    st16(rb + pos * a.r_sk, xr);
+    st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
 }
 
 template <typename T, int W>
@@ -120,9 +118,9 @@ cudaError_t run_ring(const RingArgs& a, cudaStream_t stream) {
                      host_aligned16(a.x) && host_aligned16(a.out) && host_aligned16(a.ring) &&
                      (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0 &&
                      (a.r_slot * e) % 16 == 0 && (a.r_sk * e) % 16 == 0;
-    if (vec) {
+    if (vec && a.B <= 65535) {
         const int64_t nvec = a.D / V;
-        dim3 grid((unsigned)ceil_div(nvec, kRingThreads), (unsigned)std::min<int64_t>(a.B, 65535));
+        dim3 grid((unsigned)ceil_div(nvec, kRingThreads), (unsigned)a.B);
         ring_kernel<T, W><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }

@@ -16,11 +16,6 @@ namespace {
 
 constexpr int kUnpackThreads = 64;
 
-template <typename G>
-__device__ __forceinline__ void copy_elem(const void* src, void* dst, int64_t i) {
-    reinterpret_cast<G*>(dst)[i] = reinterpret_cast<const G*>(src)[i];
-}
-
 template <typename T, int W>
 __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs a, bool bvec) {
     constexpr int V = Vec<T>::V;
@@ -55,8 +50,8 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
         st16(op, xr);
         return;
     }
-    float w[W][V], bv[V];
-    load_filter<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, bvec, w, bv);
+    uint4 wt[W], bt;
+    load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, bvec, wt, bt);
     T* sp = (T*)a.state + (int64_t)slot * a.D * K + c0 * K;
     uint4 blk[K];
 #pragma unroll
@@ -70,20 +65,21 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
             set_lane<T>(tm[k], e, lane_of<T>(blk[flat / V], flat % V));
         }
     float acc[V];
-#pragma unroll
-    for (int e = 0; e < V; ++e) acc[e] = bv[e];
+    unpack16<T>(bt, acc);
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-        float f[V];
+        float f[V], wk[V];
         unpack16<T>(tm[k], f);
+        unpack16<T>(wt[k], wk);
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], w[k][e], acc[e]);
+        for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
     }
     {
-        float f[V];
+        float f[V], wk[V];
         unpack16<T>(xr, f);
+        unpack16<T>(wt[K], wk);
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], w[K][e], acc[e]), a.silu != 0);
+        for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), a.silu != 0);
     }
     // New state: drop the oldest entry, append x.
 #pragma unroll

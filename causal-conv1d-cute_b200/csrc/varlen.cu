@@ -20,12 +20,13 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "walk.cuh"
 
 namespace cc1d {
 
 namespace {
 
-constexpr int kVarThreads = 128;
+constexpr int kVarThreads = 64;
 constexpr int kGenThreads = 256;
 
 // query_start_loc[s] clamped into [0, T].
@@ -77,67 +78,13 @@ __device__ __forceinline__ SeqSlot seq_slot(const VarArgs& a, int64_t s, bool re
 // Token-major: x rows of D adjacent channels, x_st elements apart
 // ---------------------------------------------------------------------------------------------
 
-template <typename T, int W, int U>
-__device__ __forceinline__ void walk_rows(const T* xb, int64_t x_st, T* ob, int64_t o_st,
-                                          int64_t ta, int64_t tb, float (&h)[W - 1][Vec<T>::V],
-                                          const float (&w)[W][Vec<T>::V],
-                                          const float (&bv)[Vec<T>::V], bool use_silu) {
-    constexpr int V = Vec<T>::V;
-    constexpr int K = W - 1;
-    int64_t t = ta;
-    for (; t + U <= tb; t += U) {
-        uint4 r[U];
-#pragma unroll
-        for (int i = 0; i < U; ++i) r[i] = ldg16_stream(xb + (t + i) * x_st);
-#pragma unroll
-        for (int i = 0; i < U; ++i) {
-            float xv[V], o[V];
-            unpack16<T>(r[i], xv);
-#pragma unroll
-            for (int e = 0; e < V; ++e) {
-                float acc = bv[e];
-#pragma unroll
-                for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
-                acc = fmaf(xv[e], w[K][e], acc);
-                o[e] = activate<T>(acc, use_silu);
-            }
-#pragma unroll
-            for (int k = 0; k + 1 < K; ++k)
-#pragma unroll
-                for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
-#pragma unroll
-            for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
-            st16_stream(ob + (t + i) * o_st, pack16<T>(o));
-        }
-    }
-    for (; t < tb; ++t) {
-        float xv[V], o[V];
-        unpack16<T>(ldg16_stream(xb + t * x_st), xv);
-#pragma unroll
-        for (int e = 0; e < V; ++e) {
-            float acc = bv[e];
-#pragma unroll
-            for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
-            acc = fmaf(xv[e], w[K][e], acc);
-            o[e] = activate<T>(acc, use_silu);
-        }
-#pragma unroll
-        for (int k = 0; k + 1 < K; ++k)
-#pragma unroll
-            for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
-#pragma unroll
-        for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
-        st16_stream(ob + t * o_st, pack16<T>(o));
-    }
-}
-
-template <typename T, int W, int U>
-__global__ void __launch_bounds__(kVarThreads)
+template <typename T, int W, int U, bool PF, int NT>
+__global__ void __launch_bounds__(NT)
     varlen_token_major_kernel(const VarArgs a, int strip, bool wvec, bool bvec) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
-    const int64_t j = (int64_t)blockIdx.x * kVarThreads + threadIdx.x;
+    const int64_t j = (int64_t)blockIdx.x * NT + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
     float w[W][V], bv[V];
@@ -189,7 +136,7 @@ __global__ void __launch_bounds__(kVarThreads)
 #pragma unroll
                 for (int k = 0; k < K; ++k) unpack16<T>(init[k], h[k]);
                 const int64_t end = min(eos, max(e, bos + K));
-                walk_rows<T, W, U>(xb, a.x_st, ob, a.o_st, bos, end, h, w, bv, use_silu);
+                walk_strip<T, W, U, PF>(xb, a.x_st, ob, a.o_st, bos, end, h, w, bv, use_silu);
                 if (ss.live) {
                     const int64_t n = eos - bos;
                     uint4 fin[K];
@@ -221,10 +168,8 @@ __global__ void __launch_bounds__(kVarThreads)
             } else {
                 const int64_t start = max(t, bos + K);
                 if (start < e) {
-#pragma unroll
-                    for (int k = 0; k < K; ++k)
-                        unpack16<T>(ldg16(xb + (start - K + k) * a.x_st), h[k]);
-                    walk_rows<T, W, U>(xb, a.x_st, ob, a.o_st, start, e, h, w, bv, use_silu);
+                    load_halo<T, W>(xb, a.x_st, start, h);  // rows >= bos: the sequence's own
+                    walk_strip<T, W, U, PF>(xb, a.x_st, ob, a.o_st, start, e, h, w, bv, use_silu);
                 }
             }
             t = e;
@@ -325,9 +270,9 @@ __global__ void __launch_bounds__(kGenThreads) varlen_generic_kernel(const VarAr
     }
 }
 
-// Strip length of the token-major walk: 64 tokens keeps the halo re-read under 5% at W = 4 while
-// leaving ~1e6 threads at the serving shapes.
-int varlen_strip(int64_t T) { return T <= 64 ? (int)std::max<int64_t>(T, 1) : 64; }
+// Strip length of the token-major walk, as for the channel-last prefill (fwd.cu cl_strip): 128
+// tokens re-read only 2.3% of the rows as halo at W = 4 and measured fastest on B200.
+int varlen_strip(int64_t T) { return T <= 128 ? (int)std::max<int64_t>(T, 1) : 128; }
 
 template <typename T, int W>
 cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
@@ -346,7 +291,8 @@ cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
         const int64_t nstrips = ceil_div(a.T, strip);
         const int64_t nvec = a.D / V;
         dim3 grid((unsigned)ceil_div(nvec, kVarThreads), (unsigned)std::min<int64_t>(nstrips, 65535));
-        varlen_token_major_kernel<T, W, 4><<<grid, kVarThreads, 0, stream>>>(a, strip, wvec, bvec);
+        varlen_token_major_kernel<T, W, 8, true, kVarThreads>
+            <<<grid, kVarThreads, 0, stream>>>(a, strip, wvec, bvec);
         return cudaGetLastError();
     }
     const int strip = 64;

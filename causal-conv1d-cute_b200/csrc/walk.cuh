@@ -1,0 +1,103 @@
+// Token-row walk shared by the channel-last prefill and the token-major varlen kernels.
+//
+// A thread owns one 16-byte vector of V adjacent channels and walks consecutive token rows,
+// keeping the W-1 most recent inputs of its channels in registers (fp32, oldest first).
+#pragma once
+
+#include "common.cuh"
+
+namespace cc1d {
+
+// One output vector from the fp32 window h (oldest first) and the new input xv; shifts xv into
+// the window afterwards. Bias first, taps oldest first, one fused multiply-add per tap.
+template <typename T, int W>
+__device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const float* xv,
+                                          const float (&w)[W][Vec<T>::V],
+                                          const float (&bv)[Vec<T>::V], bool use_silu,
+                                          float* o) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+        float acc = bv[e];
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
+        acc = fmaf(xv[e], w[K][e], acc);
+        o[e] = activate<T>(acc, use_silu);
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k)
+#pragma unroll
+        for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
+#pragma unroll
+    for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
+}
+
+// Walk rows [ta, tb) of one channel group: h holds the W-1 previous inputs (fp32, oldest first).
+// Rows are loaded U at a time; with PF the next U rows are requested before the current U are
+// computed, so 2U 16-byte loads per thread stay in flight (bytes in flight per SM bound this
+// kernel).
+template <typename T, int W, int U, bool PF>
+__device__ __forceinline__ void walk_strip(const T* __restrict__ xb, int64_t x_st,
+                                           T* __restrict__ ob, int64_t o_st, int64_t ta,
+                                           int64_t tb, float (&h)[W - 1][Vec<T>::V],
+                                           const float (&w)[W][Vec<T>::V],
+                                           const float (&bv)[Vec<T>::V], bool use_silu) {
+    constexpr int V = Vec<T>::V;
+    int64_t t = ta;
+    auto emit = [&](const uint4& r, int64_t row) {
+        float xv[V], o[V];
+        unpack16<T>(r, xv);
+        conv_step<T, W>(h, xv, w, bv, use_silu, o);
+        st16_stream(ob + row * o_st, pack16<T>(o));
+    };
+    if (PF) {
+        uint4 nxt[U];
+        bool have = t + U <= tb;
+        if (have) {
+#pragma unroll
+            for (int i = 0; i < U; ++i) nxt[i] = ldg16_stream(xb + (t + i) * x_st);
+        }
+        while (have) {
+            uint4 cur[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i) cur[i] = nxt[i];
+            const int64_t tn = t + U;
+            have = tn + U <= tb;
+            if (have) {
+#pragma unroll
+                for (int i = 0; i < U; ++i) nxt[i] = ldg16_stream(xb + (tn + i) * x_st);
+            }
+#pragma unroll
+            for (int i = 0; i < U; ++i) emit(cur[i], t + i);
+            t = tn;
+        }
+    } else {
+        for (; t + U <= tb; t += U) {
+            uint4 r[U];
+#pragma unroll
+            for (int i = 0; i < U; ++i) r[i] = ldg16_stream(xb + (t + i) * x_st);
+#pragma unroll
+            for (int i = 0; i < U; ++i) emit(r[i], t + i);
+        }
+    }
+    for (; t < tb; ++t) emit(ldg16_stream(xb + t * x_st), t);
+}
+
+// Window of the W-1 rows before t0 (zeros before the sequence start).
+template <typename T, int W>
+__device__ __forceinline__ void load_halo(const T* xb, int64_t x_st, int64_t t0,
+                                          float (&h)[W - 1][Vec<T>::V]) {
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k) {
+        const int64_t t = t0 - (W - 1) + k;
+        if (t >= 0) {
+            unpack16<T>(ldg16(xb + t * x_st), h[k]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < Vec<T>::V; ++e) h[k][e] = 0.f;
+        }
+    }
+}
+
+}  // namespace cc1d
