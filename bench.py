@@ -2,6 +2,7 @@
 """Benchmark of the depthwise causal conv1d hot path on B200.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-paths]
+python bench.py --profile fwd|decode|ring|spec|varlen   (4 launches of one kernel, for ncu)
 
 Headline (the configuration the metric is quoted on): prefill of
 x (batch 8, seqlen 4096, dim 8192) bf16 ~N(0,1) stored token-major and passed as its
@@ -57,6 +58,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-paths", action="store_true")
+    p.add_argument("--profile", choices=("fwd", "decode", "ring", "spec", "varlen"), default=None,
+                   help="run 4 launches of one kernel on a case larger than L2 (for ncu) and exit")
     return p.parse_args()
 
 
@@ -455,8 +458,58 @@ def sharded_check(rank, world, device):
     return bool(flag.item())
 
 
+def profile_case(case, device):
+    """A few launches of one kernel, sized for an ncu capture (a few hundred MB on the device)."""
+    import causal_conv1d_cute as C
+
+    g = torch.Generator(device=device).manual_seed(0)
+    bf = torch.bfloat16
+    w = (torch.rand(D, W, device=device, generator=g) - 0.5).to(bf)
+    b = (torch.randn(D, device=device, generator=g) * 0.1).to(bf)
+    if case == "fwd":  # config 2 with batch 2: 128 MiB in, 128 MiB out
+        x = torch.randn(2, L, D, device=device, generator=g).to(bf)
+        out = torch.empty_like(x).transpose(1, 2)
+        calls = [lambda: C.causal_conv1d_fn(x.transpose(1, 2), w, b, "silu", out=out)] * 4
+    elif case in ("decode", "ring"):  # config 3, full size
+        x = torch.randn(256, D, device=device, generator=g).to(bf)
+        if case == "decode":
+            cache = torch.randn(1024, D, 3, device=device, generator=g).to(bf)
+            idx = torch.randperm(1024, device=device, generator=g)[:256].to(torch.int32)
+            calls = [lambda: C.causal_conv1d_update(x, cache, w, b, "silu", idx)] * 4
+        else:
+            ring = torch.randn(256, 3, D, device=device, generator=g).to(bf)
+            seen = torch.randint(1, 8193, (256,), device=device, generator=g, dtype=torch.int32)
+            calls = [lambda: C.causal_conv1d_update_ring(x, ring, w, b, "silu", seen)] * 4
+    elif case == "spec":  # config 4, full size
+        xs = torch.randn(64, 4, D, device=device, generator=g).to(bf).transpose(1, 2)
+        st = torch.randn(64, D, 3, device=device, generator=g).to(bf)
+        inter = torch.empty(64, 4, D, 3, device=device, dtype=bf)
+        perm = torch.randperm(64, device=device, generator=g).to(torch.int32)
+        calls = [lambda: C.causal_conv1d_update(xs, st, w, b, "silu", perm, -1, inter, perm)] * 4
+    else:  # config 5 with 8 of its 32 lognormal sequences
+        rng = np.random.default_rng(0)
+        lens = np.clip(np.round(rng.lognormal(7, 1, 8)), 1, 8192).astype(np.int64)
+        T = int(lens.sum())
+        qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=device, dtype=torch.int32)
+        xv = torch.randn(T, D, device=device, generator=g).to(bf)
+        states = torch.randn(64, D, 3, device=device, generator=g).to(bf)
+        cidx = torch.arange(8, device=device, dtype=torch.int32) * 3
+        hinit = torch.ones(8, dtype=torch.bool, device=device)
+        calls = [lambda: C.causal_conv1d_varlen_fn(xv.t(), w, None, qsl, cidx, hinit, states, "silu")] * 4
+    # An L2-sized write between launches so every captured launch starts cold.
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
+    for f in calls:
+        flush.fill_(1)
+        f()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile": case, "launches": len(calls)}))
+
+
 def main():
     args = parse()
+    if args.profile:
+        profile_case(args.profile, torch.device("cuda", 0))
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -35,6 +35,7 @@ __global__ void __launch_bounds__(NT)
     load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
                       w, bv);
     const bool use_silu = a.silu != 0;
+    prescale_filter<T, W>(w, bv, use_silu);
     const int64_t units = (int64_t)nstrips * a.B;
     for (int64_t u = blockIdx.y; u < units; u += gridDim.y) {
         const int64_t b = u / nstrips;

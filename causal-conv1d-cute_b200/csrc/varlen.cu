@@ -78,6 +78,66 @@ __device__ __forceinline__ SeqSlot seq_slot(const VarArgs& a, int64_t s, bool re
 // Token-major: x rows of D adjacent channels, x_st elements apart
 // ---------------------------------------------------------------------------------------------
 
+// Owner work of sequence s for one channel group: read the initial state (zeros without one),
+// write the final state (the last W-1 inputs of [initial state | sequence], as raw bits) and leave
+// the initial state in the fp32 window h. The final state is written before the walk, so the
+// raw initial state does not stay live across it.
+template <typename T, int W>
+__device__ __forceinline__ void owner_state(const VarArgs& a, const T* xb, int64_t c0, int64_t s,
+                                            int64_t bos, int64_t eos, bool report,
+                                            float (&h)[W - 1][Vec<T>::V]) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    if (report) check_bounds(a, s);
+    const SeqSlot ss = seq_slot(a, s, report);
+    T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c0 * K : nullptr;
+    uint4 init[K];
+    if (ss.use_init) {
+        uint4 blk[K];
+#pragma unroll
+        for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
+#pragma unroll
+        for (int ee = 0; ee < V; ++ee)
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                const int flat = ee * K + k;
+                set_lane<T>(init[k], ee, lane_of<T>(blk[flat / V], flat % V));
+            }
+    } else {
+#pragma unroll
+        for (int k = 0; k < K; ++k) init[k] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < K; ++k) unpack16<T>(init[k], h[k]);
+    if (!ss.live) return;
+    const int64_t n = eos - bos;
+    uint4 fin[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int64_t pos = eos - K + k;
+        if (pos >= bos) {
+            fin[k] = ldg16(xb + pos * a.x_st);
+        } else {
+            // n < K: entry k + n of the initial state.
+            const int64_t m = k + n;
+            uint4 v = init[0];
+#pragma unroll
+            for (int q = 1; q < K; ++q) v = (m == q) ? init[q] : v;
+            fin[k] = v;
+        }
+    }
+    uint4 blk[K];
+#pragma unroll
+    for (int q = 0; q < K; ++q)
+#pragma unroll
+        for (int i = 0; i < V; ++i) {
+            const int flat = q * V + i;
+            set_lane<T>(blk[q], i, lane_of<T>(fin[flat % K], flat / K));
+        }
+#pragma unroll
+    for (int q = 0; q < K; ++q) st16(sp + q * V, blk[q]);
+}
+
 template <typename T, int W, int U, bool PF, int NT>
 __global__ void __launch_bounds__(NT)
     varlen_token_major_kernel(const VarArgs a, int strip, bool wvec, bool bvec) {
@@ -91,6 +151,7 @@ __global__ void __launch_bounds__(NT)
     load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
                       w, bv);
     const bool use_silu = a.silu != 0;
+    prescale_filter<T, W>(w, bv, use_silu);
     const T* xb = (const T*)a.x + c0;
     T* ob = (T*)a.out + c0;
     const int64_t nstrips = ceil_div(a.T, strip);
@@ -112,66 +173,20 @@ __global__ void __launch_bounds__(NT)
             }
             const int64_t e = min(t1, eos);
             float h[K][V];
+            int64_t ta, tb;
             if (t == bos) {
-                // Owner of sequence s.
-                if (j == 0) check_bounds(a, s);
-                const SeqSlot ss = seq_slot(a, s, j == 0);
-                T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c0 * K : nullptr;
-                uint4 init[K];
-                if (ss.use_init) {
-                    uint4 blk[K];
-#pragma unroll
-                    for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
-#pragma unroll
-                    for (int ee = 0; ee < V; ++ee)
-#pragma unroll
-                        for (int k = 0; k < K; ++k) {
-                            const int flat = ee * K + k;
-                            set_lane<T>(init[k], ee, lane_of<T>(blk[flat / V], flat % V));
-                        }
-                } else {
-#pragma unroll
-                    for (int k = 0; k < K; ++k) init[k] = make_uint4(0, 0, 0, 0);
-                }
-#pragma unroll
-                for (int k = 0; k < K; ++k) unpack16<T>(init[k], h[k]);
-                const int64_t end = min(eos, max(e, bos + K));
-                walk_strip<T, W, U, PF>(xb, a.x_st, ob, a.o_st, bos, end, h, w, bv, use_silu);
-                if (ss.live) {
-                    const int64_t n = eos - bos;
-                    uint4 fin[K];
-#pragma unroll
-                    for (int k = 0; k < K; ++k) {
-                        const int64_t pos = eos - K + k;
-                        if (pos >= bos) {
-                            fin[k] = ldg16(xb + pos * a.x_st);
-                        } else {
-                            // n < K: entry k + n of the initial state.
-                            const int64_t m = k + n;
-                            uint4 v = init[0];
-#pragma unroll
-                            for (int q = 1; q < K; ++q) v = (m == q) ? init[q] : v;
-                            fin[k] = v;
-                        }
-                    }
-                    uint4 blk[K];
-#pragma unroll
-                    for (int q = 0; q < K; ++q)
-#pragma unroll
-                        for (int i = 0; i < V; ++i) {
-                            const int flat = q * V + i;
-                            set_lane<T>(blk[q], i, lane_of<T>(fin[flat % K], flat / K));
-                        }
-#pragma unroll
-                    for (int q = 0; q < K; ++q) st16(sp + q * V, blk[q]);
-                }
+                // Owner of sequence s: initial state in, final state out, then the walk starts
+                // at the sequence start and runs past the strip end over the first W-1 tokens.
+                owner_state<T, W>(a, xb, c0, s, bos, eos, j == 0, h);
+                ta = bos;
+                tb = min(eos, max(e, bos + K));
             } else {
-                const int64_t start = max(t, bos + K);
-                if (start < e) {
-                    load_halo<T, W>(xb, a.x_st, start, h);  // rows >= bos: the sequence's own
-                    walk_strip<T, W, U, PF>(xb, a.x_st, ob, a.o_st, start, e, h, w, bv, use_silu);
-                }
+                // Tokens less than W-1 after the sequence start belong to its owner.
+                ta = max(t, bos + K);
+                tb = e;
+                if (ta < tb) load_halo<T, W>(xb, a.x_st, ta, h);  // rows >= bos
             }
+            if (ta < tb) walk_strip<T, W, U, PF>(xb, a.x_st, ob, a.o_st, ta, tb, h, w, bv, use_silu);
             t = e;
             if (e == eos) ++s;
         }

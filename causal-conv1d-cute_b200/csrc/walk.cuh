@@ -4,12 +4,45 @@
 // keeping the W-1 most recent inputs of its channels in registers (fp32, oldest first).
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace cc1d {
 
+// Scale applied to the filter and bias of the streaming kernels: with SiLU on a 16-bit output,
+// the weights are pre-multiplied by 1/2 (exact in fp32), so the accumulator holds h = a / 2 and
+// SiLU(a) = a * (tanh(a / 2) / 2 + 1/2) = h * tanh(h) + h takes one MUFU and one FMA per element.
+// The sums are exactly half of the unscaled ones (power-of-two scaling commutes with rounding
+// outside the fp32 subnormal range), so outputs are unchanged.
+template <typename T>
+__host__ __device__ constexpr bool prescaled_silu() {
+    return !std::is_same<T, float>::value;
+}
+
+template <typename T, int W>
+__device__ __forceinline__ void prescale_filter(float (&w)[W][Vec<T>::V], float (&b)[Vec<T>::V],
+                                                bool use_silu) {
+    if (prescaled_silu<T>() && use_silu) {
+#pragma unroll
+        for (int e = 0; e < Vec<T>::V; ++e) {
+#pragma unroll
+            for (int k = 0; k < W; ++k) w[k][e] *= 0.5f;
+            b[e] *= 0.5f;
+        }
+    }
+}
+
+// Activation of a prescaled accumulator (see prescale_filter).
+template <typename T>
+__device__ __forceinline__ float activate_prescaled(float acc, bool use_silu) {
+    if (prescaled_silu<T>()) return use_silu ? fmaf(acc, tanh_approx(acc), acc) : acc;
+    return activate<T>(acc, use_silu);
+}
+
 // One output vector from the fp32 window h (oldest first) and the new input xv; shifts xv into
-// the window afterwards. Bias first, taps oldest first, one fused multiply-add per tap.
+// the window afterwards. Bias first, taps oldest first, one fused multiply-add per tap. The
+// filter is prescaled (prescale_filter).
 template <typename T, int W>
 __device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const float* xv,
                                           const float (&w)[W][Vec<T>::V],
@@ -23,7 +56,7 @@ __device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const fl
 #pragma unroll
         for (int k = 0; k < K; ++k) acc = fmaf(h[k][e], w[k][e], acc);
         acc = fmaf(xv[e], w[K][e], acc);
-        o[e] = activate<T>(acc, use_silu);
+        o[e] = activate_prescaled<T>(acc, use_silu);
     }
 #pragma unroll
     for (int k = 0; k + 1 < K; ++k)
