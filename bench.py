@@ -58,7 +58,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-paths", action="store_true")
-    p.add_argument("--profile", choices=("fwd", "decode", "ring", "spec", "varlen"), default=None,
+    p.add_argument("--profile", choices=("fwd", "fwd_cf", "decode", "ring", "spec", "varlen", "varlen_cf"),
+                   default=None,
                    help="run 4 launches of one kernel on a case larger than L2 (for ncu) and exit")
     return p.parse_args()
 
@@ -331,6 +332,13 @@ def run_paths(device, reps=50, sets=8):
         res[name] = {"us_cold": cold, "us_warm": warm, "bytes": nbytes,
                      "gbs_cold": nbytes / (cold * 1e3), **(extra or {})}
 
+    # Config 2 stored channel-first: contiguous (8, 8192, 4096) (the reference's "bdl" layout).
+    xcf = torch.randn(B, D, L, device=device, generator=g).to(bf)
+    ocf = torch.empty_like(xcf)
+    us = graph_us([lambda: C.causal_conv1d_fn(xcf, w4, bias, "silu", out=ocf)], 20)
+    res["prefill_channel_first"] = {"us": us, "bytes": HEADLINE_BYTES, "gbs": HEADLINE_BYTES / (us * 1e3)}
+    del xcf, ocf
+
     # Config 3: single-token indexed decode, B=256, 1024-slot cache (48 MiB per set).
     Bd, slots = 256, 1024
     calls = []
@@ -381,6 +389,14 @@ def run_paths(device, reps=50, sets=8):
         f = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xv.t(), wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
         us = graph_us([f], 20)
         res[f"varlen_w{Wv}"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3), "tokens": T}
+        if Wv == 4:
+            # The same batch stored channel-first: contiguous (8192, T).
+            xc = xv.t().contiguous()
+            fc = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xc, wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
+            us = graph_us([fc], 20)
+            res["varlen_w4_channel_first"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3),
+                                              "tokens": T}
+            del xc
     return res
 
 
@@ -470,6 +486,10 @@ def profile_case(case, device):
         x = torch.randn(2, L, D, device=device, generator=g).to(bf)
         out = torch.empty_like(x).transpose(1, 2)
         calls = [lambda: C.causal_conv1d_fn(x.transpose(1, 2), w, b, "silu", out=out)] * 4
+    elif case == "fwd_cf":  # the same batch stored channel-first (2, 8192, 4096) contiguous
+        x = torch.randn(2, D, L, device=device, generator=g).to(bf)
+        out = torch.empty_like(x)
+        calls = [lambda: C.causal_conv1d_fn(x, w, b, "silu", out=out)] * 4
     elif case in ("decode", "ring"):  # config 3, full size
         x = torch.randn(256, D, device=device, generator=g).to(bf)
         if case == "decode":
@@ -492,6 +512,8 @@ def profile_case(case, device):
         T = int(lens.sum())
         qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=device, dtype=torch.int32)
         xv = torch.randn(T, D, device=device, generator=g).to(bf)
+        if case == "varlen_cf":  # channel-first: contiguous (8192, T); the call gets x = xv.t()
+            xv = xv.t().contiguous().t()
         states = torch.randn(64, D, 3, device=device, generator=g).to(bf)
         cidx = torch.arange(8, device=device, dtype=torch.int32) * 3
         hinit = torch.ones(8, dtype=torch.bool, device=device)

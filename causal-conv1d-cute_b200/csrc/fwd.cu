@@ -21,6 +21,7 @@ namespace {
 
 constexpr int kClThreads = 64;
 constexpr int kCfThreads = 256;
+constexpr int kCfElems = 16;  // elements per lane per iteration of the flat-stream kernel
 constexpr int kGenThreads = 256;
 
 template <typename T, int W, int U, bool PF, int NT>
@@ -49,21 +50,25 @@ __global__ void __launch_bounds__(NT)
     }
 }
 
-// Flat-stream kernel for contiguous (B, D, L) with L >= 8. Element f sits at row f / L (channel
+// Flat-stream kernel for contiguous (B, D, L) with L >= 16. Element f sits at row f / L (channel
 // (f / L) % D) and position t = f % L; tap k of its output reads element f - (W-1) + k when that
-// lies in the same row (t >= W-1-k), zero otherwise. A lane's 8 elements straddle at most one
-// row boundary, so at most two channels' weights are needed per vector.
+// lies in the same row (t >= W-1-k), zero otherwise. A lane owns EPT = 16 consecutive elements
+// (two 16-byte vectors for 16-bit types, four for fp32) and receives the W-1 elements before them
+// from the lane to its left by a warp shuffle; lane 0 gets them from lane 31 of the previous
+// iteration, so every element is read from HBM once. The next iteration's vectors are requested
+// before the current ones are computed. A lane's elements straddle at most one row boundary.
 template <typename T, int W>
 __global__ void __launch_bounds__(kCfThreads)
     fwd_channel_first_kernel(const FwdArgs a, int64_t total, int iters) {
     constexpr int K = W - 1;
-    constexpr int EPT = 8;
+    constexpr int EPT = kCfElems;
     constexpr int PER = 16 / (int)sizeof(T);
     constexpr int NV = EPT / PER;
+    constexpr int WSPAN = 32 * EPT;  // elements per warp iteration
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int64_t gw = ((int64_t)blockIdx.x * kCfThreads + threadIdx.x) >> 5;
-    const int64_t base = gw * (int64_t)iters * 256;
+    const int64_t base = gw * (int64_t)iters * WSPAN;
     if (base >= total) return;  // warp-uniform
     const T* x = (const T*)a.x;
     T* out = (T*)a.out;
@@ -83,19 +88,31 @@ __global__ void __launch_bounds__(kCfThreads)
         const int64_t p = base - K + k;
         carry[k] = (lane == 0 && p >= 0) ? to_f32<T>(x[p]) : 0.f;
     }
+    auto load = [&](int64_t g, uint4 (&v)[NV]) {
+        if (g + EPT <= total) {
+#pragma unroll
+            for (int q = 0; q < NV; ++q) v[q] = ldg16_stream(x + g + q * PER);
+        } else {
+#pragma unroll
+            for (int q = 0; q < NV; ++q) {
+                v[q] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+                for (int i = 0; i < PER; ++i)
+                    if (g + q * PER + i < total) set_lane<T>(v[q], i, x[g + q * PER + i]);
+            }
+        }
+    };
+    uint4 cur[NV];
+    load(f, cur);
     int64_t wc = -1;
     float w0[W], b0 = 0.f;
     for (int it = 0; it < iters; ++it) {
-        f = base + (int64_t)it * 256 + lane * EPT;
+        f = base + (int64_t)it * WSPAN + lane * EPT;
+        uint4 nxt[NV];
+        if (it + 1 < iters) load(f + WSPAN, nxt);
         float xv[EPT];
-        const bool full = f + EPT <= total;
-        if (full) {
 #pragma unroll
-            for (int v = 0; v < NV; ++v) unpack16<T>(ldg16_stream(x + f + v * PER), xv + v * PER);
-        } else {
-#pragma unroll
-            for (int e = 0; e < EPT; ++e) xv[e] = (f + e < total) ? to_f32<T>(x[f + e]) : 0.f;
-        }
+        for (int q = 0; q < NV; ++q) unpack16<T>(cur[q], xv + q * PER);
         float win[K + EPT];
 #pragma unroll
         for (int k = 0; k < K; ++k) {
@@ -106,48 +123,65 @@ __global__ void __launch_bounds__(kCfThreads)
         }
 #pragma unroll
         for (int e = 0; e < EPT; ++e) win[K + e] = xv[e];
+        const bool full = f + EPT <= total;
         if (f < total) {
             if (c != wc) {
                 load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c, w0, b0);
                 wc = c;
             }
-            float w1[W], b1 = 0.f;
-            const bool straddle = t + EPT > L;
-            if (straddle) {
-                const int64_t c1 = (c + 1 == D) ? 0 : c + 1;
-                load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c1, w1, b1);
-            }
             float o[EPT];
+            if (full && t >= K && t + EPT <= L) {
+                // Fast path: the elements and their W-1 predecessors lie in one row.
 #pragma unroll
-            for (int e = 0; e < EPT; ++e) {
-                const bool second = straddle && (t + e >= L);
-                const int64_t te = second ? t + e - L : t + e;
-                float acc = second ? b1 : b0;
+                for (int e = 0; e < EPT; ++e) {
+                    float acc = b0;
 #pragma unroll
-                for (int k = 0; k < W; ++k) {
-                    const float v = (te >= K - k) ? win[e + k] : 0.f;
-                    acc = fmaf(v, second ? w1[k] : w0[k], acc);
+                    for (int k = 0; k < W; ++k) acc = fmaf(win[e + k], w0[k], acc);
+                    o[e] = activate<T>(acc, use_silu);
                 }
-                o[e] = activate<T>(acc, use_silu);
-            }
-            if (full) {
 #pragma unroll
-                for (int v = 0; v < NV; ++v) st16_stream(out + f + v * PER, pack16<T>(o + v * PER));
+                for (int q = 0; q < NV; ++q) st16_stream(out + f + q * PER, pack16<T>(o + q * PER));
             } else {
+                float w1[W], b1 = 0.f;
+                const bool straddle = t + EPT > L;
+                if (straddle) {
+                    const int64_t c1 = (c + 1 == D) ? 0 : c + 1;
+                    load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c1, w1, b1);
+                }
 #pragma unroll
-                for (int e = 0; e < EPT; ++e)
-                    if (f + e < total) out[f + e] = from_f32<T>(o[e]);
+                for (int e = 0; e < EPT; ++e) {
+                    const bool second = straddle && (t + e >= L);
+                    const int64_t te = second ? t + e - L : t + e;
+                    float acc = second ? b1 : b0;
+#pragma unroll
+                    for (int k = 0; k < W; ++k) {
+                        const float v = (te >= K - k) ? win[e + k] : 0.f;
+                        acc = fmaf(v, second ? w1[k] : w0[k], acc);
+                    }
+                    o[e] = activate<T>(acc, use_silu);
+                }
+                if (full) {
+#pragma unroll
+                    for (int q = 0; q < NV; ++q)
+                        st16_stream(out + f + q * PER, pack16<T>(o + q * PER));
+                } else {
+#pragma unroll
+                    for (int e = 0; e < EPT; ++e)
+                        if (f + e < total) out[f + e] = from_f32<T>(o[e]);
+                }
             }
         }
-        // Advance this lane by one warp stride (256 elements).
-        if (L >= 256) {
-            t += 256;
-            while (t >= L) {
+#pragma unroll
+        for (int q = 0; q < NV; ++q) cur[q] = nxt[q];
+        // Advance this lane by one warp stride.
+        if (L >= WSPAN) {
+            t += WSPAN;
+            if (t >= L) {
                 t -= L;
                 c = (c + 1 == D) ? 0 : c + 1;
             }
         } else {
-            const int64_t f2 = f + 256;
+            const int64_t f2 = f + WSPAN;
             row = f2 / L;
             t = f2 - row * L;
             c = row % D;
@@ -227,9 +261,9 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     }
     const bool rows_dense = a.x_sl == 1 && a.o_sl == 1 && a.x_sd == a.L && a.o_sd == a.L &&
                             (a.B == 1 || (a.x_sb == a.D * a.L && a.o_sb == a.D * a.L));
-    if (rows_dense && a.L >= 8 && host_aligned16(a.x) && host_aligned16(a.out)) {
+    if (rows_dense && a.L >= kCfElems && host_aligned16(a.x) && host_aligned16(a.out)) {
         const int64_t total = a.B * a.D * a.L;
-        const int64_t chunks = ceil_div(total, 256);  // one warp iteration each
+        const int64_t chunks = ceil_div(total, 32 * kCfElems);  // one warp iteration each
         // Enough warps to fill every SM several times over, each walking a few chunks.
         const int iters = (int)std::max<int64_t>(1, std::min<int64_t>(8, chunks / (148 * 64)));
         const int64_t warps = ceil_div(chunks, iters);

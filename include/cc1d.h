@@ -122,8 +122,10 @@ cc1d_status_t cc1d_update_ring(const void* x, int64_t x_sb, int64_t x_sd,
                                int32_t dtype, int32_t silu, int32_t* dev_status, void* stream);
 
 /*
- * Packed variable-length prefill in ONE launch. x and out are (dim, ntokens): token-major
- * views (x_sd == 1) and channel-first storage (x_st == 1) both take vectorised kernels.
+ * Packed variable-length prefill. x and out are (dim, ntokens). Token-major views (x_sd == 1,
+ * the serving layout) take ONE vectorised launch for any number of sequences; contiguous
+ * channel-first storage (x_st == 1) takes a vectorised stream pass plus a per-(channel, sequence)
+ * boundary launch; other strides take a scalar kernel.
  * Sequence i spans tokens [query_start_loc[i], query_start_loc[i+1]); tokens outside every
  * sequence keep their previous output contents. When conv_states (nslots, dim, W-1) is given,
  * sequence i starts from conv_states[cache_indices[i]] if has_initial_state[i] != 0 (from zeros
