@@ -190,6 +190,25 @@ __device__ __forceinline__ float activate(float a, bool use_silu) {
     return use_silu ? silu<T>(a) : a;
 }
 
+// CTAs of `kern` (launched with `threads` threads, no dynamic shared memory) that the current
+// device holds at once: SM count x resident CTAs per SM. Cached per device in `cache`, an array
+// of kSlotCacheDevices zero-initialised ints owned by the caller; 0 when the query fails.
+constexpr int kSlotCacheDevices = 64;
+
+inline int device_slots(const void* kern, int threads, int* cache) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSlotCacheDevices) return 0;
+    if (cache[dev] == 0) {
+        int sms = 0, per_sm = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, 0) !=
+                cudaSuccess)
+            return 0;
+        cache[dev] = sms * per_sm;
+    }
+    return cache[dev];
+}
+
 __device__ __forceinline__ void flag_status(int32_t* status, int32_t bits) {
     if (status != nullptr) atomicOr(status, bits);
 }

@@ -2,9 +2,11 @@
 //
 // Three kernels, chosen by layout in launch_fwd:
 //   fwd_channel_last   (B, L, D) storage, token rows of D adjacent channels (x_sd == 1): every
-//                      thread owns one 16-byte vector of channels and walks a strip of tokens,
-//                      keeping the W-1 most recent inputs in registers. The strip re-reads only
-//                      the W-1 rows before it, which its neighbour strip has just pulled into L2.
+//                      thread owns one 16-byte vector of channels and walks a run of tokens,
+//                      keeping the W-1 most recent inputs in registers; a run re-reads only the
+//                      W-1 rows before it, which its neighbour has just pulled into L2. Runs are
+//                      fixed strips (several waves) or balanced shares (one wave), per the launch
+//                      table in run_fwd.
 //   fwd_channel_first  (B, D, L) contiguous storage: the tensor is one flat stream; every lane of
 //                      a warp owns 8 consecutive elements and receives the W-1 elements before
 //                      them from the lane to its left by a warp shuffle, so HBM is read once.
@@ -47,6 +49,41 @@ __global__ void __launch_bounds__(NT)
         float h[W - 1][V];
         load_halo<T, W>(xb, a.x_sl, t0, h);
         walk_strip<T, W, U, PF>(xb, a.x_sl, ob, a.o_sl, t0, t1, h, w, bv, use_silu);
+    }
+}
+
+// Balanced variant: blockIdx.x is the channel block (NT vectors) and blockIdx.y one of gridDim.y
+// equal contiguous shares of the flattened (batch, token) rows; the grid is sized to the CTAs the
+// GPU holds at once. A thread walks its channel vector through the share's rows, re-reading the
+// W-1 rows before each batch stretch. Every CTA does the same work whatever B and L are (no
+// partial last wave), and the CTAs of one share, launched back to back, read the same token rows
+// at about the same time, so each DRAM page is opened once for all its channel blocks.
+template <typename T, int W, int U, bool PF, int NT>
+__global__ void __launch_bounds__(NT)
+    fwd_channel_last_share_kernel(const FwdArgs a, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    const int64_t nvec = a.D / V;
+    const int64_t j = (int64_t)blockIdx.x * NT + threadIdx.x;
+    if (j >= nvec) return;
+    const int64_t total = a.B * a.L;
+    int64_t r = total * blockIdx.y / gridDim.y;
+    const int64_t end = total * (blockIdx.y + 1) / gridDim.y;
+    const bool use_silu = a.silu != 0;
+    const int64_t c0 = j * V;
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    prescale_filter<T, W>(w, bv, use_silu);
+    while (r < end) {
+        const int64_t b = r / a.L;
+        const int64_t t0 = r - b * a.L;
+        const int64_t n = min(end - r, a.L - t0);
+        const T* xb = (const T*)a.x + b * a.x_sb + c0;
+        T* ob = (T*)a.out + b * a.o_sb + c0;
+        float h[W - 1][V];
+        load_halo<T, W>(xb, a.x_sl, t0, h);
+        walk_strip<T, W, U, PF>(xb, a.x_sl, ob, a.o_sl, t0, t0 + n, h, w, bv, use_silu);
+        r += n;
     }
 }
 
@@ -229,16 +266,20 @@ __global__ void __launch_bounds__(kGenThreads)
     }
 }
 
-// Launch table for the channel-last strip walk: tokens per strip. Short strips give more
-// threads (latency hiding), long strips re-read fewer halo rows. Measured on B200 at
-// B=8, L=4096, D=8192 (8 rows in flight per thread, 64-thread CTAs): strips of 16 / 32 / 64 /
-// 128 / 256 tokens ran at 245 / 200 / 185 / 182 / 203 us. Short sequences use one strip.
-int cl_strip(int64_t B, int64_t L, int64_t nvec) {
-    (void)B;
-    (void)nvec;
-    if (L <= 128) return (int)std::max<int64_t>(L, 1);
-    return 128;
-}
+// Launch table for the channel-last walk: strips (one CTA row per (batch, strip of at most
+// kStripRows tokens), scheduled by the hardware in several waves) or balanced shares (one wave of
+// resident CTAs, equal work each). Measured on B200 (bf16, 64-thread CTAs, 8 rows in flight per
+// thread, L2 flushed between launches), strips / balanced:
+//   shape (B x L x D)        W = 2              W = 4              W = 8
+//   8 x 4096 x 8192     182.5 / 196.6 us   193.3 / 190.4 us   251.1 / 224.5 us
+//   4 x 2048 x 8192      53.8 /  55.8 us    67.7 /  59.1 us    76.4 /  71.5 us
+//   3 x 1000 x 2304      22.6 /  16.5 us    24.5 /  14.5 us    30.6 /  20.5 us
+//   64 x 128 x 4096      33.0 /  33.7 us    33.8 /  35.7 us    38.9 /  44.9 us
+// Strips win for W = 2 (the lightest walk, where the scheduler's dynamic balancing across SMs is
+// worth more than a strip restart) and for short sequences (a share would restart its walk at every
+// sequence), as long as they give at least half a wave of CTAs; otherwise balanced shares.
+constexpr int64_t kStripRows = 128;
+constexpr int64_t kMinShareRows = 16;
 
 template <typename T, int W>
 cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
@@ -251,12 +292,22 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
                     (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0;
     if (cl) {
         const int64_t nvec = a.D / V;
-        const int strip = cl_strip(a.B, a.L, nvec);
-        const int nstrips = (int)ceil_div(a.L, strip);
-        const int64_t units = (int64_t)nstrips * a.B;
-        dim3 grid((unsigned)ceil_div(nvec, kClThreads), (unsigned)std::min<int64_t>(units, 65535));
-        fwd_channel_last_kernel<T, W, 8, true, kClThreads>
-            <<<grid, kClThreads, 0, stream>>>(a, strip, nstrips, wvec, bvec);
+        const int64_t gx = ceil_div(nvec, (int64_t)kClThreads);
+        static int slot_cache[kSlotCacheDevices] = {};
+        auto share = fwd_channel_last_share_kernel<T, W, 8, true, kClThreads>;
+        const int64_t slots = device_slots((const void*)share, kClThreads, slot_cache);
+        const int64_t strip = std::max<int64_t>(1, std::min<int64_t>(a.L, kStripRows));
+        const int64_t nstrips = ceil_div(a.L, strip);
+        if ((W == 2 || a.L <= kStripRows) && a.B * nstrips * gx * 2 >= slots) {
+            dim3 grid((unsigned)gx, (unsigned)std::min<int64_t>(a.B * nstrips, 65535));
+            fwd_channel_last_kernel<T, W, 8, true, kClThreads>
+                <<<grid, kClThreads, 0, stream>>>(a, (int)strip, (int)nstrips, wvec, bvec);
+            return cudaGetLastError();
+        }
+        const int64_t gy = std::max<int64_t>(
+            1, std::min<int64_t>({std::max<int64_t>(slots, 1) / gx,
+                                  ceil_div(a.B * a.L, kMinShareRows), 65535}));
+        share<<<dim3((unsigned)gx, (unsigned)gy), kClThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     const bool rows_dense = a.x_sl == 1 && a.o_sl == 1 && a.x_sd == a.L && a.o_sd == a.L &&

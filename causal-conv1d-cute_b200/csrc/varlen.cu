@@ -143,7 +143,7 @@ __device__ __forceinline__ void owner_state(const VarArgs& a, const T* xb, int64
 
 template <typename T, int W, int U, bool PF, int NT>
 __global__ void __launch_bounds__(NT)
-    varlen_token_major_kernel(const VarArgs a, int strip, bool wvec, bool bvec) {
+    varlen_token_major_kernel(const VarArgs a, bool wvec, bool bvec) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
@@ -157,10 +157,10 @@ __global__ void __launch_bounds__(NT)
     prescale_filter<T, W>(w, bv, use_silu);
     const T* xb = (const T*)a.x + c0;
     T* ob = (T*)a.out + c0;
-    const int64_t nstrips = ceil_div(a.T, strip);
-    for (int64_t u = blockIdx.y; u < nstrips; u += gridDim.y) {
-        const int64_t t0 = u * strip;
-        const int64_t t1 = min(t0 + strip, a.T);
+    // This CTA's share of the packed tokens: [t0, t1), one of gridDim.y equal parts.
+    {
+        const int64_t t0 = a.T * blockIdx.y / gridDim.y;
+        const int64_t t1 = a.T * (blockIdx.y + 1) / gridDim.y;
         int64_t s = seq_of(a, t0);
         int64_t t = t0;
         if (s < 0) {
@@ -558,9 +558,15 @@ __global__ void __launch_bounds__(kGenThreads) varlen_generic_kernel(const VarAr
     }
 }
 
-// Strip length of the token-major walk, as for the channel-last prefill (fwd.cu cl_strip): 128
-// tokens re-read only 2.3% of the rows as halo at W = 4 and measured fastest on B200.
-int varlen_strip(int64_t T) { return T <= 128 ? (int)std::max<int64_t>(T, 1) : 128; }
+// Token shares of the token-major walk, as for the channel-last prefill (fwd.cu): strips of at most
+// kStripTokens tokens for W = 2, else one balanced wave of resident CTAs. Measured on B200 with the
+// config-5 batch (32 lognormal sequences, 40807 tokens x 8192 channels, bf16):
+//   width                       2          3          4          8
+//   128-token strips         219.9 us   248 us     232.2 us   304.6 us
+//   one balanced wave        232.2 us   225.6 us   230.5 us   258.4 us
+// From W = 3 on a share saves the per-strip halo, owner and sequence-search work that grows with W.
+constexpr int64_t kStripTokens = 128;
+constexpr int64_t kMinShareTokens = 16;
 
 template <typename T, int W>
 cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
@@ -575,12 +581,17 @@ cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
     const bool tm = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
                     host_aligned16(a.out) && (a.x_st * e) % 16 == 0 && (a.o_st * e) % 16 == 0;
     if (tm && sok) {
-        const int strip = varlen_strip(a.T);
-        const int64_t nstrips = ceil_div(a.T, strip);
-        const int64_t nvec = a.D / V;
-        dim3 grid((unsigned)ceil_div(nvec, kVarThreads), (unsigned)std::min<int64_t>(nstrips, 65535));
-        varlen_token_major_kernel<T, W, 8, true, kVarThreads>
-            <<<grid, kVarThreads, 0, stream>>>(a, strip, wvec, bvec);
+        const int64_t gx = ceil_div(a.D / V, (int64_t)kVarThreads);
+        static int slot_cache[kSlotCacheDevices] = {};
+        auto kern = varlen_token_major_kernel<T, W, 8, true, kVarThreads>;
+        const int64_t slots = device_slots((const void*)kern, kVarThreads, slot_cache);
+        const int64_t strips = ceil_div(a.T, kStripTokens);
+        const int64_t shares = W == 2 && strips * gx * 2 >= slots
+                                   ? strips
+                                   : std::min<int64_t>(std::max<int64_t>(slots, 1) / gx,
+                                                       ceil_div(a.T, kMinShareTokens));
+        const int64_t gy = std::max<int64_t>(1, std::min<int64_t>(shares, 65535));
+        kern<<<dim3((unsigned)gx, (unsigned)gy), kVarThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     const bool cf = a.x_st == 1 && a.o_st == 1 && a.x_sd == a.T && a.o_sd == a.T && a.T >= kCfElems &&
