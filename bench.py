@@ -48,6 +48,8 @@ METRIC = "prefill/varlen achieved HBM GB/s vs ~8 TB/s; decode µs/call at bs=256
 B, L, D, W = 8, 4096, 8192, 4
 E = 2  # bf16
 HEADLINE_BYTES = 2 * B * L * D * E + D * W * E + D * E  # 1,073,823,744
+# The kernel the headline call dispatches to (balanced shares: W = 4, 4096-token sequences).
+HEADLINE_KERNEL = "fwd_channel_last_share_kernel"
 L2_BYTES = 126 * 2**20
 
 
@@ -249,7 +251,7 @@ def run_headline(args, rank, world, device):
     e2e_value = HEADLINE_BYTES * world * e2e_steps / (e2e_ms / 1e3) / 1e9
     achieved = HEADLINE_BYTES / (avg_launch_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
-    traffic = profiled_traffic("fwd_channel_last_kernel")
+    traffic = profiled_traffic(HEADLINE_KERNEL)
     return {
         "value": value,
         "ms_per_step": total_ms / args.steps,
@@ -268,7 +270,7 @@ def run_headline(args, rank, world, device):
             "frac": achieved / peak,
             "traffic": traffic,
             "peak_source": f"{peak_kind} hbm_gbs (copy, burst)",
-            "kernel": "fwd_channel_last_kernel",
+            "kernel": HEADLINE_KERNEL,
             "algorithmic_bytes_per_launch": HEADLINE_BYTES,
             "avg_launch_us": avg_launch_ms * 1e3,
         },

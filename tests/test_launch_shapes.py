@@ -1,0 +1,101 @@
+"""Shapes that reach each launch form of the token-row walks.
+
+The channel-last prefill and the token-major varlen kernels run either as fixed strips over
+several waves or as one wave of balanced shares, chosen on the host from the width, the sequence
+lengths and the GPU's resident-CTA count. These cases sit on both sides of that choice, with shares
+that cross batch and sequence boundaries and a partial last channel block, and check that the
+result is bit-identical to the scalar path (the same arithmetic in the same order, reached by
+viewing rows of a wider buffer that are not 16-byte aligned), and, for a small case, to the oracle.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from _util import assert_bits, assert_close, to_np
+from causal_conv1d_cute import causal_conv1d_fn, causal_conv1d_varlen_fn
+
+PAD = -1
+
+# (B, L, D, W): W = 2 strips over many CTAs; short sequences (one strip each, enough CTAs);
+# balanced shares crossing batch boundaries; shares with a partial channel block; long shares.
+FWD_SHAPES = [
+    (8, 1000, 8192, 2),
+    (64, 100, 4096, 4),
+    (5, 37, 512, 4),
+    (3, 1000, 2304, 8),
+    (2, 5000, 1024, 3),
+    (1, 17, 64, 6),
+]
+
+
+def _unaligned_view(t, D):
+    """(B, L, D) tensor -> a view with the same values whose rows are 2 bytes past 16-byte lines."""
+    B, L, _ = t.shape
+    wide = torch.empty(B, L, D + 1, device=t.device, dtype=t.dtype)
+    v = wide[:, :, 1:]
+    v.copy_(t)
+    return v
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B,L,D,W", FWD_SHAPES)
+def test_prefill_launch_forms_match_scalar_path(B, L, D, W):
+    g = torch.Generator(device="cuda").manual_seed(B * 7919 + L * 31 + W)
+    x = torch.randn(B, L, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.rand(D, W, device="cuda", generator=g) - 0.5).to(torch.bfloat16)
+    b = (torch.randn(D, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    y = causal_conv1d_fn(x.transpose(1, 2), w, b, "silu")
+    ys = causal_conv1d_fn(_unaligned_view(x, D).transpose(1, 2), w, b, "silu")
+    torch.cuda.synchronize()
+    assert torch.equal(y, ys)
+    if B * L * D <= 1 << 20:
+        ref = oracle.fwd(to_np(x.transpose(1, 2)), to_np(w), to_np(b), True, "bf16")
+        assert_close(y, ref, torch.bfloat16)
+
+
+# (lengths, D, W): many short sequences (strips at W = 2), lognormal lengths with balanced shares
+# at W = 3 and 8, and sequences shorter than W - 1 inside a share.
+def _lengths(seed, n, mean):
+    rng = np.random.default_rng(seed)
+    return [int(v) for v in np.clip(np.round(rng.lognormal(mean, 1.0, n)), 1, 6000)]
+
+
+VARLEN_CASES = [
+    (_lengths(1, 400, 4.0), 2048, 2),
+    (_lengths(2, 32, 7.0), 512, 3),
+    (_lengths(3, 32, 7.0), 768, 8),
+    ([1, 2, 3, 0, 9, 1, 700, 2, 5], 1024, 8),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", range(len(VARLEN_CASES)))
+def test_varlen_launch_forms_match_scalar_path(case):
+    lens, D, W = VARLEN_CASES[case]
+    K, nseq = W - 1, len(lens)
+    g = torch.Generator(device="cuda").manual_seed(case)
+    qsl = torch.tensor([0] + list(np.cumsum(lens)), device="cuda", dtype=torch.int32)
+    T = int(qsl[-1])
+    slots = nseq + 2
+    cidx = torch.randperm(slots, device="cuda", generator=g)[:nseq].to(torch.int32)
+    cidx[::7] = PAD
+    hinit = torch.rand(nseq, device="cuda", generator=g) < 0.5
+    x = torch.randn(T, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = (torch.rand(D, W, device="cuda", generator=g) - 0.5).to(torch.bfloat16)
+    st0 = torch.randn(slots, D, K, device="cuda", dtype=torch.bfloat16, generator=g)
+    st = st0.clone()
+    y = causal_conv1d_varlen_fn(x.t(), w, None, qsl, cidx, hinit, st, "silu")
+    sts = st0.clone()
+    xs = _unaligned_view(x.unsqueeze(0), D)[0]
+    ys = causal_conv1d_varlen_fn(xs.t(), w, None, qsl, cidx, hinit, sts, "silu")
+    torch.cuda.synchronize()
+    assert torch.equal(y, ys)
+    assert torch.equal(st, sts)
+    if T * D <= 1 << 21:
+        r_out, r_st = oracle.varlen(to_np(x.t()), to_np(w), None, to_np(qsl), to_np(cidx),
+                                    to_np(hinit), to_np(st0), True, PAD, "bf16")
+        mask = ~np.isnan(r_out)
+        assert_close(to_np(y), np.nan_to_num(r_out), torch.bfloat16, mask)
+        assert_bits(st, r_st)
