@@ -58,8 +58,8 @@ __global__ void __launch_bounds__(NT)
 // W-1 rows before each batch stretch. Every CTA does the same work whatever B and L are (no
 // partial last wave), and the CTAs of one share, launched back to back, read the same token rows
 // at about the same time, so each DRAM page is opened once for all its channel blocks.
-template <typename T, int W, int U, bool PF, int NT>
-__global__ void __launch_bounds__(NT)
+template <typename T, int W, int U, bool PF, int NT, int MINB>
+__global__ void __launch_bounds__(NT, MINB)
     fwd_channel_last_share_kernel(const FwdArgs a, bool wvec, bool bvec) {
     constexpr int V = Vec<T>::V;
     const int64_t nvec = a.D / V;
@@ -268,18 +268,32 @@ __global__ void __launch_bounds__(kGenThreads)
 
 // Launch table for the channel-last walk: strips (one CTA row per (batch, strip of at most
 // kStripRows tokens), scheduled by the hardware in several waves) or balanced shares (one wave of
-// resident CTAs, equal work each). Measured on B200 (bf16, 64-thread CTAs, 8 rows in flight per
-// thread, L2 flushed between launches), strips / balanced:
+// resident CTAs, equal work each). Measured on B200 (bf16, 64-thread CTAs), strips / balanced:
 //   shape (B x L x D)        W = 2              W = 4              W = 8
 //   8 x 4096 x 8192     182.5 / 196.6 us   193.3 / 190.4 us   251.1 / 224.5 us
 //   4 x 2048 x 8192      53.8 /  55.8 us    67.7 /  59.1 us    76.4 /  71.5 us
 //   3 x 1000 x 2304      22.6 /  16.5 us    24.5 /  14.5 us    30.6 /  20.5 us
 //   64 x 128 x 4096      33.0 /  33.7 us    33.8 /  35.7 us    38.9 /  44.9 us
-// Strips win for W = 2 (the lightest walk, where the scheduler's dynamic balancing across SMs is
-// worth more than a strip restart) and for short sequences (a share would restart its walk at every
-// sequence), as long as they give at least half a wave of CTAs; otherwise balanced shares.
+// (L2 flushed between launches.) Strips win for W <= 3 (the lightest walks, where the scheduler's
+// dynamic balancing across SMs is worth more than a strip restart; W = 3 at the config-2 shape:
+// 178.0 vs 199.1 us) and for short sequences (a share would restart its walk at every sequence),
+// as long as they give at least half a wave of CTAs; otherwise balanced shares.
 constexpr int64_t kStripRows = 128;
 constexpr int64_t kMinShareRows = 16;
+
+// Rows in flight per thread (U) and minimum resident CTAs per SM in the launch bounds of the
+// balanced walk (0: the compiler's own register budget). Measured on B200 at the config-2 shape,
+// one launch at a time (W: us for U = 8 with the compiler's budget / U = 8 with minimum 1 /
+// U = 6 with minimum 1): 4: 182.6 / 196.2 / 183.1; 5: 200.5 / 197.4 / 184.4;
+// 6: 204.6 / 201.6 / 218.7; 7: 206.1 / 202.1 / 219.3; 8: 217.9 / 207.7 / 227.0.
+template <int W>
+constexpr int share_rows() {
+    return W == 5 ? 6 : 8;
+}
+template <int W>
+constexpr int share_min_ctas() {
+    return W >= 5 ? 1 : 0;
+}
 
 template <typename T, int W>
 cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
@@ -294,11 +308,12 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
         const int64_t nvec = a.D / V;
         const int64_t gx = ceil_div(nvec, (int64_t)kClThreads);
         static int slot_cache[kSlotCacheDevices] = {};
-        auto share = fwd_channel_last_share_kernel<T, W, 8, true, kClThreads>;
+        auto share = fwd_channel_last_share_kernel<T, W, share_rows<W>(), true, kClThreads,
+                                                   share_min_ctas<W>()>;
         const int64_t slots = device_slots((const void*)share, kClThreads, slot_cache);
         const int64_t strip = std::max<int64_t>(1, std::min<int64_t>(a.L, kStripRows));
         const int64_t nstrips = ceil_div(a.L, strip);
-        if ((W == 2 || a.L <= kStripRows) && a.B * nstrips * gx * 2 >= slots) {
+        if ((W <= 3 || a.L <= kStripRows) && a.B * nstrips * gx * 2 >= slots) {
             dim3 grid((unsigned)gx, (unsigned)std::min<int64_t>(a.B * nstrips, 65535));
             fwd_channel_last_kernel<T, W, 8, true, kClThreads>
                 <<<grid, kClThreads, 0, stream>>>(a, (int)strip, (int)nstrips, wvec, bvec);

@@ -35,12 +35,14 @@ __global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bo
     // One row per thread (gridDim.y == B) and raw weights widened at use: a lean thread keeps
     // twice as many of them resident.
     const int64_t b = blockIdx.y;
+    // The slot load heads the dependent chain (slot -> ring rows): issue it first.
+    const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
+    const int32_t seen = __ldg(a.seen + b);
     uint4 wt[W], bt;
     load_filter_raw<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
                           bvec, wt, bt);
     const uint4 xr = ldg16((const T*)a.x + b * a.x_sb + c0);
-    const int pos = ring_pos(__ldg(a.seen + b), K);
-    const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
+    const int pos = ring_pos(seen, K);
     if (slot == a.pad) return;
     if (slot < 0 || (int64_t)slot >= a.nslots) {
         if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);

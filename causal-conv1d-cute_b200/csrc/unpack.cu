@@ -24,6 +24,8 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
     const int64_t bi = blockIdx.y;
     const int64_t G = a.D / V, GZ = a.zdim / V;
     const T* qrow = (const T*)a.qkvz + bi * a.q_sb;
+    // The slot load heads the dependent chain (slot -> state): issue it before the copies.
+    const int32_t slot = j < G ? __ldg(a.idx + bi) : 0;
     if (j < GZ) {
         const uint4 zr = ldg16(qrow + a.D + j * V);
         st16((T*)a.z + bi * a.zdim + j * V, zr);
@@ -45,7 +47,6 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
     const int64_t c0 = j * V;
     const uint4 xr = ldg16(qrow + c0);
     T* op = (T*)a.out + bi * a.D + c0;
-    const int32_t slot = __ldg(a.idx + bi);
     if (slot == a.pad || slot < 0 || (int64_t)slot >= a.nslots) {
         st16(op, xr);
         return;

@@ -153,6 +153,8 @@ __global__ void __launch_bounds__(kUpdThreads)
     if (j >= nvec) return;
     const int64_t c0 = j * V;
     const int64_t b = blockIdx.y;
+    // The slot load heads the dependent chain (slot -> state block): issue it first.
+    const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
     uint4 wt[W], bt;
     load_filter_raw<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
                           bvec, wt, bt);
@@ -161,7 +163,6 @@ __global__ void __launch_bounds__(kUpdThreads)
 #pragma unroll
     for (int t = 0; t < LMAX; ++t)
         if (t < a.L) xr[t] = ldg16(xb + t * a.x_st);
-    const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
     if (slot == a.pad) return;
     if (slot < 0 || (int64_t)slot >= a.nslots) {
         if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
@@ -176,64 +177,68 @@ __global__ void __launch_bounds__(kUpdThreads)
 }
 
 // Single-step decode without per-step states, the serving hot case, kept lean: one row per
-// thread, raw tap-major weights widened at use, no runtime step loop. At 47 registers about twice
-// as many threads are resident as with the general kernel, which measured 8.7 us instead of
-// 10.5 us per call at B = 256, D = 8192 on B200 (CUDA-graph replay, cold L2).
-template <typename T, int W, int SS>
-__global__ void __launch_bounds__(kUpdThreads) decode1_kernel(const UpdArgs a) {
+// thread, raw tap-major weights widened at use, no runtime step loop (the general kernel's 90
+// registers halve the resident threads). Every load is issued before any compute, the slot load
+// first since it heads the only dependent chain (slot -> state); a row with the pad slot or a
+// slot outside the cache skips the state load and all stores. CHECK (a status word was given)
+// adds the report of slots outside the cache, which costs 0.35 us per call, so the unchecked
+// variant leaves it out. Measured on B200 at B = 256, D = 8192 (CUDA-graph replay, cold L2):
+// 8.25 us per call unchecked; 9.4 us with the state load placed behind the slot checks.
+template <typename T, int W, int SS, bool CHECK>
+__global__ void __launch_bounds__(kUpdThreads, 1) decode1_kernel(const UpdArgs a) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
     const int64_t j = (int64_t)blockIdx.x * kUpdThreads + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
-    uint4 wt[W], bt;
-    load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, a.bias != nullptr,
-                          wt, bt);
-    const bool use_silu = a.silu != 0;
     // One row per thread (gridDim.y == B): a row loop would let the compiler widen the invariant
     // weights once and keep them in 40 fp32 registers.
     const int64_t b = blockIdx.y;
-    {
-        const uint4 xr = ldg16((const T*)a.x + b * a.x_sb + c0);
-        const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
-        if (slot == a.pad) return;
-        if (slot < 0 || (int64_t)slot >= a.nslots) {
-            if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
-            return;
-        }
-        T* sp = (T*)a.state + (int64_t)slot * a.s_slot + c0 * SS;
-        uint4 sr[SS];
+    const int32_t slot = b < a.B ? (a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b) : a.pad;
+    uint4 wt[W], bt;
+    load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, a.bias != nullptr,
+                          wt, bt);
+    uint4 xr;
+    if (b < a.B) xr = ldg16((const T*)a.x + b * a.x_sb + c0);
+    const bool live = slot != a.pad && slot >= 0 && (int64_t)slot < a.nslots;
+    uint4 sr[SS];
+    if (live) {
+        const T* sp = (const T*)a.state + (int64_t)slot * a.s_slot + c0 * SS;
 #pragma unroll
         for (int q = 0; q < SS; ++q) sr[q] = ld16(sp + q * V);
-        uint4 win[SS];
-        block_to_time<T, SS>(sr, win);
-        float acc[V];
-        unpack16<T>(bt, acc);
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            float f[V], wk[V];
-            unpack16<T>(win[SS - K + k], f);
-            unpack16<T>(wt[k], wk);
-#pragma unroll
-            for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
-        }
-        {
-            float f[V], wk[V];
-            unpack16<T>(xr, f);
-            unpack16<T>(wt[K], wk);
-#pragma unroll
-            for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), use_silu);
-        }
-        st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
-#pragma unroll
-        for (int s = 0; s + 1 < SS; ++s) win[s] = win[s + 1];
-        win[SS - 1] = xr;
-        uint4 blk[SS];
-        time_to_block<T, SS>(win, blk);
-#pragma unroll
-        for (int q = 0; q < SS; ++q) st16(sp + q * V, blk[q]);
     }
+    if (CHECK && !live && slot != a.pad && j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+    if (!live) return;
+    const bool use_silu = a.silu != 0;
+    uint4 win[SS];
+    block_to_time<T, SS>(sr, win);
+    float acc[V];
+    unpack16<T>(bt, acc);
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        float f[V], wk[V];
+        unpack16<T>(win[SS - K + k], f);
+        unpack16<T>(wt[k], wk);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
+    }
+    {
+        float f[V], wk[V];
+        unpack16<T>(xr, f);
+        unpack16<T>(wt[K], wk);
+#pragma unroll
+        for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), use_silu);
+    }
+    st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
+#pragma unroll
+    for (int s = 0; s + 1 < SS; ++s) win[s] = win[s + 1];
+    win[SS - 1] = xr;
+    uint4 blk[SS];
+    time_to_block<T, SS>(win, blk);
+    T* sp = (T*)a.state + (int64_t)slot * a.s_slot + c0 * SS;
+#pragma unroll
+    for (int q = 0; q < SS; ++q) st16(sp + q * V, blk[q]);
 }
 
 // Any strides, any state length S >= W-1 (the whole row shifts by L), any per-step layout.
@@ -331,8 +336,13 @@ cudaError_t run_update(const UpdArgs& a, cudaStream_t stream) {
     if (xok && sok && iok && lean && (a.S == K || a.S == P) && a.B <= 65535) {
         const int64_t nvec = a.D / V;
         dim3 grid((unsigned)ceil_div(nvec, kUpdThreads), (unsigned)a.B);
-        if (a.S == K) decode1_kernel<T, W, K><<<grid, kUpdThreads, 0, stream>>>(a);
-        else decode1_kernel<T, W, P><<<grid, kUpdThreads, 0, stream>>>(a);
+        if (a.status != nullptr) {
+            if (a.S == K) decode1_kernel<T, W, K, true><<<grid, kUpdThreads, 0, stream>>>(a);
+            else decode1_kernel<T, W, P, true><<<grid, kUpdThreads, 0, stream>>>(a);
+        } else {
+            if (a.S == K) decode1_kernel<T, W, K, false><<<grid, kUpdThreads, 0, stream>>>(a);
+            else decode1_kernel<T, W, P, false><<<grid, kUpdThreads, 0, stream>>>(a);
+        }
         return cudaGetLastError();
     }
     if (xok && sok && iok && a.L >= 1 && a.L <= 16 && a.B <= 65535) {

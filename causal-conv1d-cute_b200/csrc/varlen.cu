@@ -141,8 +141,8 @@ __device__ __forceinline__ void owner_state(const VarArgs& a, const T* xb, int64
     for (int q = 0; q < K; ++q) st16(sp + q * V, blk[q]);
 }
 
-template <typename T, int W, int U, bool PF, int NT>
-__global__ void __launch_bounds__(NT)
+template <typename T, int W, int U, bool PF, int NT, int MINB>
+__global__ void __launch_bounds__(NT, MINB)
     varlen_token_major_kernel(const VarArgs a, bool wvec, bool bvec) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
@@ -568,6 +568,19 @@ __global__ void __launch_bounds__(kGenThreads) varlen_generic_kernel(const VarAr
 constexpr int64_t kStripTokens = 128;
 constexpr int64_t kMinShareTokens = 16;
 
+// Rows in flight per thread (U) and minimum resident CTAs per SM in the launch bounds of the
+// token-major walk. Measured on B200 with the config-5 batch, one balanced wave (W: us with
+// U = 8 / U = 6, minimum 1 CTA; U = 6 with minimum 6 CTAs): 4: 230.4 / 231.2; 5: 244.6 / 231.1;
+// 6: 248.3 / 268.0, 236.2 with minimum 6; 8: 256.1 / 278.3.
+template <int W>
+constexpr int var_rows() {
+    return W == 5 || W == 6 ? 6 : 8;
+}
+template <int W>
+constexpr int var_min_ctas() {
+    return W == 6 ? 6 : 0;  // 0: no minimum, the compiler's own register budget
+}
+
 template <typename T, int W>
 cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
     constexpr int V = Vec<T>::V;
@@ -583,7 +596,8 @@ cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
     if (tm && sok) {
         const int64_t gx = ceil_div(a.D / V, (int64_t)kVarThreads);
         static int slot_cache[kSlotCacheDevices] = {};
-        auto kern = varlen_token_major_kernel<T, W, 8, true, kVarThreads>;
+        auto kern =
+            varlen_token_major_kernel<T, W, var_rows<W>(), true, kVarThreads, var_min_ctas<W>()>;
         const int64_t slots = device_slots((const void*)kern, kVarThreads, slot_cache);
         const int64_t strips = ceil_div(a.T, kStripTokens);
         const int64_t shares = W == 2 && strips * gx * 2 >= slots

@@ -145,3 +145,34 @@ def test_slot_outside_cache_is_skipped_and_reported(request):
     assert device_status() == 1
     assert torch.equal(st[[1, 3, 4, 5]], st0[[1, 3, 4, 5]])
     assert torch.equal(st[0], torch.cat([st0[0][:, 1:], x[0].unsqueeze(-1)], 1))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("W,padded", [(4, False), (2, False), (8, True)])
+def test_unchecked_decode_matches_checked(W, padded):
+    """With the status word off the decode runs a variant without the slot report; it must give
+    the same outputs and states bit for bit, skip the pad slot and slots outside the cache alike."""
+    from causal_conv1d_cute import set_device_checks
+
+    D, B, slots = 2048, 64, 80
+    g = torch.Generator(device="cuda").manual_seed(W)
+    x = torch.randn(B, D, device="cuda", dtype=torch.bfloat16, generator=g)
+    w = torch.randn(D, W, device="cuda", dtype=torch.bfloat16, generator=g)
+    b = torch.randn(D, device="cuda", dtype=torch.bfloat16, generator=g)
+    S = 8 if padded else W - 1
+    st0 = torch.randn(slots, D, S, device="cuda", dtype=torch.bfloat16, generator=g)
+    idx = torch.randperm(slots, device="cuda", generator=g)[:B].to(torch.int32)
+    idx[5] = -1
+    st_on, st_off = st0.clone(), st0.clone()
+    out_on = causal_conv1d_update(x, st_on, w, b, "silu", conv_state_indices=idx)
+    set_device_checks(False)
+    try:
+        out_off = causal_conv1d_update(x, st_off, w, b, "silu", conv_state_indices=idx)
+    finally:
+        set_device_checks(True)
+    torch.cuda.synchronize()
+    live = idx >= 0
+    assert torch.equal(out_on[live], out_off[live])
+    assert torch.equal(st_on, st_off)
+    assert torch.equal(st_off[~torch.isin(torch.arange(slots, device="cuda"), idx)],
+                       st0[~torch.isin(torch.arange(slots, device="cuda"), idx)])
