@@ -16,10 +16,11 @@ rank r owns channels [8192 r, 8192 (r + 1)) of a layer with 8192 N channels, so 
 fixed (weak scaling) and the kernels exchange nothing. NCCL is used once, after timing, to
 all-gather a sample of every rank's outputs and compare them bit for bit with the unsharded run.
 
-With N = 1 the other BASELINE paths are measured too ("paths"): indexed decode (config 3) and its
-ring variant, the 4-step speculative verify with dense per-step states (config 4), and packed
-varlen prefill (config 5) at widths 2, 3, 4 and 8, each replayed in a CUDA graph (no host
-launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
+With N = 1 the other BASELINE paths are measured too ("paths"): config 2 stored channel-first,
+config 2 with initial and final states and with sequence ids (the Dao-interface extras), indexed
+decode (config 3) and its ring variant, the 4-step speculative verify with dense per-step states
+(config 4), and packed varlen prefill (config 5) at widths 2, 3, 4 and 8, each replayed in a CUDA
+graph (no host launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
 exceeds L2, and "warm" repeats one set.
 
 --impl reference times the reference's CPU algorithm (the C port of its PyTorch fallback,
@@ -340,6 +341,21 @@ def run_paths(device, reps=50, sets=8):
     us = graph_us([lambda: C.causal_conv1d_fn(xcf, w4, bias, "silu", out=ocf)], 20)
     res["prefill_channel_first"] = {"us": us, "bytes": HEADLINE_BYTES, "gbs": HEADLINE_BYTES / (us * 1e3)}
     del xcf, ocf
+
+    # Config 2 with the Dao-interface extras: initial states in, final states out (channel-last
+    # states, as upstream allocates them). Algorithmic bytes add 2 * B * D * 3 elements.
+    xs = torch.randn(B, L, D, device=device, generator=g).to(bf).transpose(1, 2)
+    init = torch.randn(B, 3, D, device=device, generator=g).to(bf).transpose(1, 2)
+    fin = torch.empty_like(init)
+    nbytes = HEADLINE_BYTES + 2 * B * D * 3 * 2
+    us = graph_us([lambda: C.causal_conv1d_fwd_states(xs, w4, bias, None, init, True, fin, "silu")], 20)
+    res["prefill_states"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3)}
+    seq = torch.zeros(B, L, device=device, dtype=torch.int32)
+    seq[:, L // 2:] = 1
+    us = graph_us([lambda: C.causal_conv1d_fwd_states(xs, w4, bias, seq, None, False, None, "silu")], 20)
+    nbytes = HEADLINE_BYTES + B * L * 4
+    res["prefill_seq_idx"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3)}
+    del xs, init, fin, seq
 
     # Config 3: single-token indexed decode, B=256, 1024-slot cache (48 MiB per set).
     Bd, slots = 256, 1024

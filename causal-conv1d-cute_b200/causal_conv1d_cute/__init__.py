@@ -7,6 +7,10 @@ Public API (same names and signatures as the reference package):
   causal_conv1d_update_ring single-token decode on a ring conv state; to_ring / from_ring convert
   causal_conv1d_varlen_fn   packed variable-length prefill with an in-place conv-state cache
   supported                 whether the kernels serve a call
+
+Beyond the reference:
+  causal_conv1d_fwd_states  prefill with the Dao-AILab extras (seq_idx, initial_states, final
+                            states), which dao_compat serves instead of passing them upstream
   CausalConv1d              layer object
 
 Every entry point runs hand-written CUDA kernels from libcc1d.so (C ABI: include/cc1d.h). There is
@@ -20,6 +24,7 @@ from .api import CausalConv1d
 from .functional import (
     Unsupported,
     causal_conv1d_fn,
+    causal_conv1d_fwd_states,
     causal_conv1d_update,
     causal_conv1d_update_ring,
     causal_conv1d_varlen_fn,
@@ -31,6 +36,7 @@ __all__ = [
     "CausalConv1d",
     "Unsupported",
     "causal_conv1d_fn",
+    "causal_conv1d_fwd_states",
     "causal_conv1d_update",
     "causal_conv1d_update_ring",
     "causal_conv1d_varlen_fn",

@@ -25,6 +25,9 @@ _i32 = ctypes.c_int32
 SIGNATURES = {
     "cc1d_fwd": [_p, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64,
                  _i64, _i64, _i64, _i32, _i32, _i32, _p],
+    "cc1d_fwd_states": [_p, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _i64,
+                        _p, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i64,
+                        _i64, _i64, _i64, _i32, _i32, _i32, _p],
     "cc1d_update": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p, _i64, _i64,
                     _p, _i64, _p, _i64, _i64, _i64, _p, _i32, _p, _i64, _i64, _i64, _i64, _i64,
                     _p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p],

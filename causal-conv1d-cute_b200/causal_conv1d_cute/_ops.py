@@ -78,6 +78,29 @@ def fwd(x, weight, bias, silu, out):
     return out
 
 
+def fwd_states(x, weight, bias, silu, out, seq_idx, initial_states, final_states):
+    """Prefill with sequence ids and/or initial / final states (cc1d_fwd_states).
+
+    seq_idx int32 (batch, seqlen) or None; initial_states / final_states (batch, dim, W-1) or None.
+    """
+    lib = load()
+    B, D, L = x.shape
+    q = (None, 0, 0) if seq_idx is None else (seq_idx.data_ptr(), *seq_idx.stride())
+    i = (None, 0, 0, 0) if initial_states is None else (initial_states.data_ptr(), *initial_states.stride())
+    f = (None, 0, 0, 0) if final_states is None else (final_states.data_ptr(), *final_states.stride())
+    check(
+        lib.cc1d_fwd_states(
+            x.data_ptr(), x.stride(0), x.stride(1), x.stride(2),
+            weight.data_ptr(), weight.stride(0), weight.stride(1),
+            _ptr(bias), 0 if bias is None else bias.stride(0),
+            out.data_ptr(), out.stride(0), out.stride(1), out.stride(2),
+            *q, *i, *f,
+            B, D, L, weight.shape[1], dtype_code(x.dtype), int(bool(silu)), _stream(x.device),
+        )
+    )
+    return out
+
+
 def update(x3, state, weight, bias, silu, out3, idx, pad, inter, iidx):
     """Decode of x3 (batch, dim, steps) into out3 of the same shape (cc1d_update).
 
@@ -172,6 +195,6 @@ def update_unpack(qkvz, ba, state, weight, bias, out, z, b, a, idx, heads, silu,
 
 
 __all__ = [
-    "device_status", "fwd", "set_device_checks", "update", "update_ring", "update_unpack",
+    "device_status", "fwd", "fwd_states", "set_device_checks", "update", "update_ring", "update_unpack",
     "varlen", "_lib",
 ]

@@ -5,8 +5,9 @@ mamba_ssm, flash-linear-attention and the fast paths of Hugging Face transformer
 ``causal_conv1d.causal_conv1d_fn`` and ``causal_conv1d.causal_conv1d_update``. install() wraps both
 and rebinds them in every module that already imported them. The wrappers keep the upstream
 signatures and pass a call on to the upstream function whenever it needs something these kernels
-do not provide: gradients, seq_idx, initial_states, return_final_states, a circular state through
-cache_seqlens, a multi-token update, or tensors the kernels cannot serve. stats counts both
+do not provide: gradients, a circular state through cache_seqlens, a multi-token update, or
+tensors the kernels cannot serve. seq_idx, initial_states and return_final_states / final_states_out
+are served by causal_conv1d_fwd_states (the reference passes them upstream). stats counts both
 outcomes.
 """
 
@@ -35,15 +36,17 @@ def around_fn(
     final_states_out=None,
     activation=None,
 ):
-    """Serve causal_conv1d_fn or pass the call upstream (dao_compat.py:28-78)."""
+    """Serve causal_conv1d_fn or pass the call upstream (dao_compat.py:28-78).
+
+    Calls with seq_idx, initial_states or final states are served here too (the reference passes
+    them upstream), unless they combine seq_idx with states, which upstream rejects.
+    """
     served = (
-        seq_idx is None
-        and initial_states is None
-        and not return_final_states
-        and activation in (None, "silu", "swish")
+        activation in (None, "silu", "swish")
         and x.dim() == 3
-        and not _needs_grad(x, weight, bias)
+        and not _needs_grad(x, weight, bias, initial_states)
         and fn.supported(x, weight, bias)
+        and not (seq_idx is not None and (initial_states is not None or return_final_states))
     )
     if not served:
         stats["fn_fallback"] += 1
@@ -58,7 +61,11 @@ def around_fn(
             activation=activation,
         )
     stats["fn_fast"] += 1
-    return fn.causal_conv1d_fn(x, weight, bias, activation)
+    if seq_idx is None and initial_states is None and not return_final_states:
+        return fn.causal_conv1d_fn(x, weight, bias, activation)
+    return fn.causal_conv1d_fwd_states(
+        x, weight, bias, seq_idx, initial_states, return_final_states, final_states_out, activation
+    )
 
 
 def around_update(

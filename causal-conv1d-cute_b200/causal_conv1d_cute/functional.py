@@ -237,6 +237,77 @@ def causal_conv1d_fn(x, weight, bias=None, activation=None, out=None):
     return _layer(weight, bias, act).fwd(x, out=out)
 
 
+def causal_conv1d_fwd_states(
+    x,
+    weight,
+    bias=None,
+    seq_idx=None,
+    initial_states=None,
+    return_final_states=False,
+    final_states_out=None,
+    activation=None,
+):
+    """Prefill with the Dao-AILab causal_conv1d_fn extras, which the reference's dao_compat shim
+    passes upstream (dao_compat.py:28-78); upstream signature and results.
+
+    Args:
+        x: (batch, dim, seqlen), any strides.
+        weight: (dim, width), width 2..8; bias: optional (dim,).
+        seq_idx: optional int (batch, seqlen) sequence ids: a tap reaches back only to tokens of
+            the same id (packed sequences inside one row). Excludes the two state arguments.
+        initial_states: optional (batch, dim, width - 1): the inputs before token 0 of each row.
+        return_final_states: also return the last width - 1 inputs of [initial_states | x] per
+            row, (batch, dim, width - 1).
+        final_states_out: optional (batch, dim, width - 1) tensor to write the final states to;
+            must not overlap initial_states.
+        activation: None, "silu" or "swish".
+
+    Returns:
+        out, or (out, final_states) with return_final_states. out has x's layout (as
+        causal_conv1d_fn); allocated final states view (batch, width - 1, dim) storage, as
+        upstream.
+
+    Raises:
+        ValueError: inconsistent shapes or dtypes, seq_idx with states, overlapping states.
+        Unsupported: the kernels cannot serve the call.
+    """
+    _check(x, weight, bias, 1)
+    if x.dim() != 3:
+        raise ValueError(f"input must have shape (batch, dim, seqlen), got {tuple(x.shape)}")
+    act = _act(activation)
+    why = _reason(x, weight, bias)
+    if why is None and initial_states is not None and torch.is_grad_enabled() and initial_states.requires_grad:
+        why = "gradients are required and the kernels have no backward pass"
+    if why is not None:
+        _unsupported(why)
+    B, D, L = x.shape
+    K = weight.shape[1] - 1
+    if seq_idx is not None:
+        if initial_states is not None or return_final_states:
+            raise ValueError("seq_idx excludes initial_states and return_final_states")
+        if tuple(seq_idx.shape) != (B, L):
+            raise ValueError(f"seq_idx must have shape {(B, L)}, got {tuple(seq_idx.shape)}")
+        seq_idx = _int32(_device(seq_idx, x.device), x.device)
+    for name, st in (("initial_states", initial_states), ("final_states_out", final_states_out)):
+        if st is not None and (tuple(st.shape) != (B, D, K) or st.dtype != x.dtype or st.device != x.device):
+            raise ValueError(f"{name} must be a {x.dtype} tensor of shape {(B, D, K)} on {x.device}")
+    final = None
+    if return_final_states:
+        final = final_states_out
+        if final is None:
+            final = torch.empty((B, K, D), dtype=x.dtype, device=x.device).transpose(1, 2)
+        elif initial_states is not None and (
+            final.untyped_storage().data_ptr() == initial_states.untyped_storage().data_ptr()
+        ):
+            raise ValueError("final_states_out must not share storage with initial_states")
+    if x.stride(1) == 1 and D > 1:
+        out = torch.empty((B, L, D), dtype=x.dtype, device=x.device).transpose(1, 2)
+    else:
+        out = torch.empty((B, D, L), dtype=x.dtype, device=x.device)
+    _ops.fwd_states(x, weight, bias, act, out, seq_idx, initial_states, final)
+    return (out, final) if return_final_states else out
+
+
 def causal_conv1d_varlen_fn(
     x,
     weight,

@@ -58,6 +58,18 @@ cc1d_status_t bind_stream(void* stream) {
     return CC1D_OK;
 }
 
+// Bytes spanned by a (n0, n1, n2) tensor with non-negative element strides.
+int64_t span_bytes(int64_t n0, int64_t s0, int64_t n1, int64_t s1, int64_t n2, int64_t s2,
+                   int64_t esize) {
+    return ((n0 - 1) * s0 + (n1 - 1) * s1 + (n2 - 1) * s2 + 1) * esize;
+}
+
+bool overlap(const void* p, int64_t np, const void* q, int64_t nq) {
+    const char* a = (const char*)p;
+    const char* b = (const char*)q;
+    return a < b + nq && b < a + np;
+}
+
 }  // namespace
 
 extern "C" {
@@ -95,6 +107,42 @@ cc1d_status_t cc1d_fwd(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_sl,
                     out, o_sb, o_sd, o_sl, batch, dim, seqlen, silu != 0};
     if (cc1d_status_t s = bind_stream(stream)) return s;
     return from_cuda(cc1d::launch_fwd(a, width, dtype, (cudaStream_t)stream), "cc1d_fwd");
+}
+
+cc1d_status_t cc1d_fwd_states(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_sl,
+                              const void* weight, int64_t w_sd, int64_t w_sk,
+                              const void* bias, int64_t bias_s,
+                              void* out, int64_t o_sb, int64_t o_sd, int64_t o_sl,
+                              const int32_t* seq_idx, int64_t q_sb, int64_t q_sl,
+                              const void* initial_states, int64_t i_sb, int64_t i_sd, int64_t i_sk,
+                              void* final_states, int64_t f_sb, int64_t f_sd, int64_t f_sk,
+                              int64_t batch, int64_t dim, int64_t seqlen, int32_t width,
+                              int32_t dtype, int32_t silu, void* stream) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (batch < 0 || dim < 0 || seqlen < 0)
+        return fail(CC1D_ERR_INVALID, "negative size (batch %lld, dim %lld, seqlen %lld)",
+                    (long long)batch, (long long)dim, (long long)seqlen);
+    if (seq_idx != nullptr && (initial_states != nullptr || final_states != nullptr))
+        return fail(CC1D_ERR_INVALID, "sequence ids exclude initial and final states");
+    if (batch == 0 || dim == 0) return ok();
+    if (weight == nullptr || (seqlen > 0 && (x == nullptr || out == nullptr)))
+        return fail(CC1D_ERR_INVALID, "x, weight and out must not be NULL");
+    if (i_sb < 0 || i_sd < 0 || i_sk < 0 || f_sb < 0 || f_sd < 0 || f_sk < 0)
+        return fail(CC1D_ERR_LAYOUT, "state strides must not be negative");
+    const int64_t e = dtype == CC1D_F32 ? 4 : 2;
+    const int64_t K = width - 1;
+    if (final_states != nullptr && initial_states != nullptr &&
+        overlap(final_states, span_bytes(batch, f_sb, dim, f_sd, K, f_sk, e), initial_states,
+                span_bytes(batch, i_sb, dim, i_sd, K, i_sk, e)))
+        return fail(CC1D_ERR_INVALID, "final states overlap the initial states");
+    cc1d::FwdStateArgs a{{x, x_sb, x_sd, x_sl, weight, w_sd, w_sk, bias, bias_s,
+                          out, o_sb, o_sd, o_sl, batch, dim, seqlen, silu != 0},
+                         seq_idx, q_sb, q_sl, initial_states, i_sb, i_sd, i_sk,
+                         final_states, f_sb, f_sd, f_sk};
+    if (seqlen == 0 && final_states == nullptr) return ok();
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_fwd_states(a, width, dtype, (cudaStream_t)stream),
+                     "cc1d_fwd_states");
 }
 
 cc1d_status_t cc1d_update(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_st,

@@ -1,0 +1,270 @@
+// Prefill with initial states, final states and per-token sequence ids: the arguments of the
+// Dao-AILab causal_conv1d_fn interface (seq_idx, initial_states, return_final_states /
+// final_states_out) that the reference's dao_compat shim passes upstream (dao_compat.py:28-78).
+//
+// out[b, c, t] = act(bias[c] + sum_k w[c, k] * v(b, c, t - (W-1) + k)) where v(b, c, p) is
+//   x[b, c, p]                       for 0 <= p (and seq[b, p] == seq[b, t] with sequence ids),
+//   init[b, c, (W-1) + p]            for p < 0 with initial states,
+//   0                                otherwise;
+// a tap whose sequence id differs from the token's adds nothing (the term is skipped, not
+// multiplied by zero). final[b, c, k] = the k-th of the last W-1 entries of [init[b, c, :] | x[b, c, :]]
+// (zeros in place of init without initial states), copied bit for bit from the inputs.
+//
+// Two kernels:
+//   fwd_states_vec_kernel   channel-last x / out (16-byte channel vectors, as fwd_channel_last):
+//                           a thread walks a strip of tokens of one 16-byte channel group; the
+//                           first strip of a row takes its history from the initial states, the
+//                           last strip of a row writes the final states.
+//   fwd_states_generic_kernel  any strides, one channel of a strip per thread.
+#include <algorithm>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "walk.cuh"
+
+namespace cc1d {
+
+namespace {
+
+constexpr int kStThreads = 64;
+constexpr int kStGenThreads = 256;
+constexpr int64_t kStStrip = 128;
+constexpr int kStRows = 8;  // rows loaded together per thread
+
+// The W-1 entries of history before token t0 of row b, channels c0..c0+V-1, as fp32 (oldest
+// first): x rows for t >= 0, initial states (or zeros) for t < 0; with sequence ids, the id of
+// each history row (rows before the start carry no id: their values are 0 or initial states, and
+// sequence ids exclude initial states).
+template <typename T, int W>
+__device__ __forceinline__ void states_halo(const FwdStateArgs& a, int64_t b, int64_t c0,
+                                            int64_t t0, float (&h)[W - 1][Vec<T>::V],
+                                            int32_t (&qh)[W > 1 ? W - 1 : 1]) {
+    constexpr int V = Vec<T>::V;
+    const T* xb = (const T*)a.f.x + b * a.f.x_sb + c0;
+    const T* init = (const T*)a.init;
+#pragma unroll
+    for (int k = 0; k < W - 1; ++k) {
+        const int64_t t = t0 - (W - 1) + k;
+        if (t >= 0) {
+            unpack16<T>(ldg16(xb + t * a.f.x_sl), h[k]);
+            qh[k] = a.seq != nullptr ? __ldg(a.seq + b * a.q_sb + t * a.q_sl) : 0;
+        } else {
+#pragma unroll
+            for (int e = 0; e < V; ++e)
+                h[k][e] = init != nullptr
+                              ? to_f32<T>(init[b * a.i_sb + (c0 + e) * a.i_sd + ((W - 1) + t) * a.i_sk])
+                              : 0.f;
+            qh[k] = INT32_MIN;  // no id: the value is 0 or an initial state, never masked in
+        }
+    }
+}
+
+// Final states of row b, channels c0..c0+V-1: raw copies of x rows L-(W-1)..L-1, or of the
+// initial states (zeros without them) for positions before the row start.
+template <typename T, int W>
+__device__ __forceinline__ void states_final(const FwdStateArgs& a, int64_t b, int64_t c0, int nch) {
+    const T* xb = (const T*)a.f.x + b * a.f.x_sb;
+    const T* init = (const T*)a.init;
+    T* fin = (T*)a.fin;
+    for (int k = 0; k < W - 1; ++k) {
+        const int64_t t = a.f.L - (W - 1) + k;
+        for (int e = 0; e < nch; ++e) {
+            const int64_t c = c0 + e;
+            T v;
+            if (t >= 0) {
+                v = xb[c * a.f.x_sd + t * a.f.x_sl];
+            } else if (init != nullptr) {
+                v = init[b * a.i_sb + c * a.i_sd + ((W - 1) + t) * a.i_sk];
+            } else {
+                v = from_f32<T>(0.f);
+            }
+            fin[b * a.f_sb + c * a.f_sd + k * a.f_sk] = v;
+        }
+    }
+}
+
+// One output vector with sequence-id masking: a history tap counts only when its id equals the
+// token's id; the bias first, taps oldest first, the current token always counts.
+template <typename T, int W, bool SEQ>
+__device__ __forceinline__ void states_step(float (&h)[W - 1][Vec<T>::V],
+                                            int32_t (&qh)[W > 1 ? W - 1 : 1], const float* xv,
+                                            int32_t q, const float (&w)[W][Vec<T>::V],
+                                            const float (&bv)[Vec<T>::V], bool use_silu,
+                                            float* o) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    if (!SEQ) {
+        conv_step<T, W>(h, xv, w, bv, use_silu, o);
+        return;
+    }
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+        float acc = bv[e];
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = qh[k] == q ? fmaf(h[k][e], w[k][e], acc) : acc;
+        acc = fmaf(xv[e], w[K][e], acc);
+        o[e] = activate_prescaled<T>(acc, use_silu);
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k) {
+        qh[k] = qh[k + 1];
+#pragma unroll
+        for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
+    }
+    if (K > 0) {
+        qh[K - 1] = q;
+#pragma unroll
+        for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
+    }
+}
+
+template <typename T, int W, bool SEQ>
+__global__ void __launch_bounds__(kStThreads)
+    fwd_states_vec_kernel(const FwdStateArgs a, int64_t nstrips, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    const FwdArgs& f = a.f;
+    const int64_t nvec = f.D / V;
+    const int64_t j = (int64_t)blockIdx.x * kStThreads + threadIdx.x;
+    if (j >= nvec) return;
+    const int64_t c0 = j * V;
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)f.w, f.w_sd, f.w_sk, (const T*)f.bias, f.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = f.silu != 0;
+    prescale_filter<T, W>(w, bv, use_silu);
+    const int64_t units = nstrips * f.B;
+    for (int64_t u = blockIdx.y; u < units; u += gridDim.y) {
+        const int64_t b = u / nstrips;
+        const int64_t t0 = (u - b * nstrips) * kStStrip;
+        const int64_t t1 = min(t0 + kStStrip, f.L);
+        const T* xb = (const T*)f.x + b * f.x_sb + c0;
+        T* ob = (T*)f.out + b * f.o_sb + c0;
+        const int32_t* qb = SEQ ? a.seq + b * a.q_sb : nullptr;
+        float h[W - 1][V];
+        int32_t qh[W > 1 ? W - 1 : 1];
+        states_halo<T, W>(a, b, c0, t0, h, qh);
+        for (int64_t t = t0; t < t1; t += kStRows) {
+            uint4 r[kStRows];
+            int32_t q[kStRows];
+#pragma unroll
+            for (int i = 0; i < kStRows; ++i) {
+                if (t + i < t1) {
+                    r[i] = ldg16_stream(xb + (t + i) * f.x_sl);
+                    q[i] = SEQ ? __ldg(qb + (t + i) * a.q_sl) : 0;
+                }
+            }
+#pragma unroll
+            for (int i = 0; i < kStRows; ++i) {
+                if (t + i < t1) {
+                    float xv[V], o[V];
+                    unpack16<T>(r[i], xv);
+                    states_step<T, W, SEQ>(h, qh, xv, q[i], w, bv, use_silu, o);
+                    st16_stream(ob + (t + i) * f.o_sl, pack16<T>(o));
+                }
+            }
+        }
+        if (a.fin != nullptr && t1 == f.L) states_final<T, W>(a, b, c0, V);
+    }
+}
+
+// Any strides: thread = (row, channel, strip of kStStrip tokens).
+template <typename T, int W>
+__global__ void __launch_bounds__(kStGenThreads) fwd_states_generic_kernel(const FwdStateArgs a,
+                                                                           int64_t nstrips) {
+    constexpr int K = W - 1;
+    const FwdArgs& f = a.f;
+    const int64_t n = f.B * f.D * nstrips;
+    const bool use_silu = f.silu != 0;
+    const T* init = (const T*)a.init;
+    for (int64_t id = (int64_t)blockIdx.x * kStGenThreads + threadIdx.x; id < n;
+         id += (int64_t)gridDim.x * kStGenThreads) {
+        const int64_t s = id % nstrips;
+        const int64_t c = (id / nstrips) % f.D;
+        const int64_t b = id / (nstrips * f.D);
+        const int64_t t0 = s * kStStrip, t1 = min(t0 + kStStrip, f.L);
+        float w[W], bb;
+        load_filter1<T, W>((const T*)f.w, f.w_sd, f.w_sk, (const T*)f.bias, f.bias_s, c, w, bb);
+        const T* xr = (const T*)f.x + b * f.x_sb + c * f.x_sd;
+        T* orow = (T*)f.out + b * f.o_sb + c * f.o_sd;
+        const int32_t* qb = a.seq != nullptr ? a.seq + b * a.q_sb : nullptr;
+        float h[K > 0 ? K : 1];
+        int32_t qh[K > 0 ? K : 1];
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int64_t t = t0 - K + k;
+            if (t >= 0) {
+                h[k] = to_f32<T>(xr[t * f.x_sl]);
+                qh[k] = qb != nullptr ? qb[t * a.q_sl] : 0;
+            } else {
+                h[k] = init != nullptr ? to_f32<T>(init[b * a.i_sb + c * a.i_sd + (K + t) * a.i_sk])
+                                       : 0.f;
+                qh[k] = INT32_MIN;
+            }
+        }
+        for (int64_t t = t0; t < t1; ++t) {
+            const float xv = to_f32<T>(xr[t * f.x_sl]);
+            const int32_t q = qb != nullptr ? qb[t * a.q_sl] : 0;
+            float acc = bb;
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+                acc = (qb == nullptr || qh[k] == q) ? fmaf(h[k], w[k], acc) : acc;
+            acc = fmaf(xv, w[K], acc);
+            orow[t * f.o_sl] = from_f32<T>(activate<T>(acc, use_silu));
+#pragma unroll
+            for (int k = 0; k + 1 < K; ++k) {
+                h[k] = h[k + 1];
+                qh[k] = qh[k + 1];
+            }
+            if (K > 0) {
+                h[K - 1] = xv;
+                qh[K - 1] = q;
+            }
+        }
+        if (a.fin != nullptr && t1 == f.L) {
+            T* fin = (T*)a.fin;
+            for (int k = 0; k < K; ++k) {
+                const int64_t t = f.L - K + k;
+                T v = t >= 0 ? xr[t * f.x_sl]
+                             : (init != nullptr ? init[b * a.i_sb + c * a.i_sd + (K + t) * a.i_sk]
+                                                : from_f32<T>(0.f));
+                fin[b * a.f_sb + c * a.f_sd + k * a.f_sk] = v;
+            }
+        }
+    }
+}
+
+template <typename T, int W>
+cudaError_t run_fwd_states(const FwdStateArgs& a, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    const FwdArgs& f = a.f;
+    const int64_t e = sizeof(T);
+    const int64_t nstrips = ceil_div(std::max<int64_t>(f.L, 1), kStStrip);
+    const bool wvec = f.w_sd == W && f.w_sk == 1 && host_aligned16(f.w);
+    const bool bvec = f.bias != nullptr && f.bias_s == 1 && host_aligned16(f.bias);
+    const bool cl = f.x_sd == 1 && f.o_sd == 1 && f.D % V == 0 && host_aligned16(f.x) &&
+                    host_aligned16(f.out) && (f.x_sl * e) % 16 == 0 && (f.o_sl * e) % 16 == 0 &&
+                    (f.x_sb * e) % 16 == 0 && (f.o_sb * e) % 16 == 0;
+    if (cl) {
+        dim3 grid((unsigned)ceil_div(f.D / V, (int64_t)kStThreads),
+                  (unsigned)std::min<int64_t>(nstrips * f.B, 65535));
+        if (a.seq != nullptr)
+            fwd_states_vec_kernel<T, W, true><<<grid, kStThreads, 0, stream>>>(a, nstrips, wvec, bvec);
+        else
+            fwd_states_vec_kernel<T, W, false><<<grid, kStThreads, 0, stream>>>(a, nstrips, wvec, bvec);
+        return cudaGetLastError();
+    }
+    const int64_t n = f.B * f.D * nstrips;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, kStGenThreads), 148 * 32));
+    fwd_states_generic_kernel<T, W><<<(unsigned)blocks, kStGenThreads, 0, stream>>>(a, nstrips);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_fwd_states(const FwdStateArgs& a, int width, int dtype, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_fwd_states<T, kW>(a, stream))));
+    return err;
+}
+
+}  // namespace cc1d

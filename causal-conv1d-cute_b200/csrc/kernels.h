@@ -21,6 +21,19 @@ struct FwdArgs {
     int silu;
 };
 
+// Prefill with the Dao-interface extras: per-token sequence ids (taps reach back only to tokens
+// with the same id), initial states (the W-1 inputs before token 0 of each batch row) and final
+// states (the last W-1 inputs of [initial | x] of each row). Each pointer may be NULL.
+struct FwdStateArgs {
+    FwdArgs f;
+    const int32_t* seq;
+    int64_t q_sb, q_sl;
+    const void* init;
+    int64_t i_sb, i_sd, i_sk;
+    void* fin;
+    int64_t f_sb, f_sd, f_sk;
+};
+
 struct UpdArgs {
     const void* x;
     int64_t x_sb, x_sd, x_st;
@@ -104,6 +117,7 @@ struct UnpackArgs {
 };
 
 cudaError_t launch_fwd(const FwdArgs& a, int width, int dtype, cudaStream_t stream);
+cudaError_t launch_fwd_states(const FwdStateArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_update(const UpdArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_ring(const RingArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_varlen(const VarArgs& a, int width, int dtype, cudaStream_t stream);

@@ -77,6 +77,30 @@ cc1d_status_t cc1d_fwd(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_sl,
                        int32_t dtype, int32_t silu, void* stream);
 
 /*
+ * Prefill with the Dao-AILab causal_conv1d_fn extras. Shapes and x / weight / bias / out as in
+ * cc1d_fwd, plus (each may be NULL):
+ *   seq_idx         int32 (batch, seqlen), strides (q_sb, q_sl): a tap reaches back only to
+ *                   tokens with the same id as the output token (a different id adds nothing);
+ *   initial_states  (batch, dim, W-1), strides (i_sb, i_sd, i_sk): the W-1 inputs before token 0
+ *                   of each row (zeros when NULL);
+ *   final_states    (batch, dim, W-1), strides (f_sb, f_sd, f_sk), written: the last W-1 entries
+ *                   of [initial_states | x] of each row, bit for bit (seqlen may be 0).
+ * seq_idx excludes both states (as upstream); final_states must not overlap initial_states.
+ * Replaces: the upstream causal_conv1d_fn(x, weight, bias, seq_idx, initial_states,
+ * return_final_states, final_states_out, activation) that dao_compat.around_fn passes these
+ * calls to (dao_compat.py:28-78).
+ */
+cc1d_status_t cc1d_fwd_states(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_sl,
+                              const void* weight, int64_t w_sd, int64_t w_sk,
+                              const void* bias, int64_t bias_s,
+                              void* out, int64_t o_sb, int64_t o_sd, int64_t o_sl,
+                              const int32_t* seq_idx, int64_t q_sb, int64_t q_sl,
+                              const void* initial_states, int64_t i_sb, int64_t i_sd, int64_t i_sk,
+                              void* final_states, int64_t f_sb, int64_t f_sd, int64_t f_sk,
+                              int64_t batch, int64_t dim, int64_t seqlen, int32_t width,
+                              int32_t dtype, int32_t silu, void* stream);
+
+/*
  * Decode of `steps` tokens per batch row (1..16) against a conv-state cache updated in place.
  * x and out are (batch, dim, steps). state is (nslots, dim, state_len) with state_len >= W-1:
  * the last W-1 entries of a channel row are the history, and the whole row shifts left by

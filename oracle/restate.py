@@ -63,6 +63,43 @@ def fwd(x, w, b, silu, dtype):
     return out
 
 
+def fwd_states(x, w, b, seq_idx, init, silu, dtype):
+    """Prefill with the Dao-AILab causal_conv1d_fn extras, which the reference passes upstream
+    (dao_compat.py:28-78) to the `causal_conv1d` package (Dao-AILab/causal-conv1d; the reference
+    pins no version).
+
+    Restates that package's published semantics. x (batch, dim, seqlen); init (batch, dim, W-1)
+    or None: the history before token 0 of each row, as the reference's own varlen fallback uses a
+    cached initial state (fallback.py:77-114); the final state is the last W-1 entries of
+    [init | x]. seq_idx (batch, seqlen) or None: the output at token t sums only the taps whose
+    token has the same id as t (a differing id contributes nothing), zero history before token 0;
+    it excludes init. Returns (out rounded to dtype, final states (batch, dim, W-1)).
+    """
+    B, D, L = x.shape
+    W = w.shape[1]
+    K = W - 1
+    out = np.empty((B, D, L), np.float32)
+    final = np.empty((B, D, K), np.float32)
+    for i in range(B):
+        hist = np.zeros((D, K), np.float32) if init is None else np.asarray(init[i], np.float32)
+        full = np.concatenate([hist, x[i]], axis=1)
+        final[i] = full[:, -K:]
+        if seq_idx is None:
+            out[i] = round_to(_conv_valid(full, w, b, silu), dtype)
+            continue
+        q = np.asarray(seq_idx[i])
+        acc = np.zeros((D, L), np.float64)
+        if b is not None:
+            acc += np.asarray(b, np.float64)[:, None]
+        for t in range(L):
+            for k in range(W):
+                p = t - K + k
+                if p >= 0 and q[p] == q[t]:
+                    acc[:, t] += np.asarray(w[:, k], np.float64) * np.float64(x[i][:, p])
+        out[i] = round_to(_silu(acc) if silu else acc, dtype)
+    return out, final
+
+
 def varlen(x, w, b, qsl, cidx, hinit, states, silu, pad, dtype):
     """Packed prefill: fallback.varlen (fallback.py:77-114).
 
