@@ -11,10 +11,11 @@
 // (zeros in place of init without initial states), copied bit for bit from the inputs.
 //
 // Two kernels:
-//   fwd_states_vec_kernel   channel-last x / out (16-byte channel vectors, as fwd_channel_last):
-//                           a thread walks a strip of tokens of one 16-byte channel group; the
-//                           first strip of a row takes its history from the initial states, the
-//                           last strip of a row writes the final states.
+//   fwd_states_vec_kernel   channel-last x / out (16-byte channel vectors, the walk and grid of
+//                           the plain channel-last prefill): a thread walks a share of token
+//                           rows of one 16-byte channel group; a stretch that starts a row takes
+//                           its history from the initial states, the one that ends it writes the
+//                           final states.
 //   fwd_states_generic_kernel  any strides, one channel of a strip per thread.
 #include <algorithm>
 
@@ -29,7 +30,7 @@ namespace {
 constexpr int kStThreads = 64;
 constexpr int kStGenThreads = 256;
 constexpr int64_t kStStrip = 128;
-constexpr int kStRows = 8;  // rows loaded together per thread
+constexpr int kStRows = 8;  // rows in flight per thread (U of the walk)
 
 // The W-1 entries of history before token t0 of row b, channels c0..c0+V-1, as fp32 (oldest
 // first): x rows for t >= 0, initial states (or zeros) for t < 0; with sequence ids, the id of
@@ -38,7 +39,7 @@ constexpr int kStRows = 8;  // rows loaded together per thread
 template <typename T, int W>
 __device__ __forceinline__ void states_halo(const FwdStateArgs& a, int64_t b, int64_t c0,
                                             int64_t t0, float (&h)[W - 1][Vec<T>::V],
-                                            int32_t (&qh)[W > 1 ? W - 1 : 1]) {
+                                            int32_t (&qh)[W - 1]) {
     constexpr int V = Vec<T>::V;
     const T* xb = (const T*)a.f.x + b * a.f.x_sb + c0;
     const T* init = (const T*)a.init;
@@ -83,44 +84,13 @@ __device__ __forceinline__ void states_final(const FwdStateArgs& a, int64_t b, i
     }
 }
 
-// One output vector with sequence-id masking: a history tap counts only when its id equals the
-// token's id; the bias first, taps oldest first, the current token always counts.
-template <typename T, int W, bool SEQ>
-__device__ __forceinline__ void states_step(float (&h)[W - 1][Vec<T>::V],
-                                            int32_t (&qh)[W > 1 ? W - 1 : 1], const float* xv,
-                                            int32_t q, const float (&w)[W][Vec<T>::V],
-                                            const float (&bv)[Vec<T>::V], bool use_silu,
-                                            float* o) {
-    constexpr int V = Vec<T>::V;
-    constexpr int K = W - 1;
-    if (!SEQ) {
-        conv_step<T, W>(h, xv, w, bv, use_silu, o);
-        return;
-    }
-#pragma unroll
-    for (int e = 0; e < V; ++e) {
-        float acc = bv[e];
-#pragma unroll
-        for (int k = 0; k < K; ++k) acc = qh[k] == q ? fmaf(h[k][e], w[k][e], acc) : acc;
-        acc = fmaf(xv[e], w[K][e], acc);
-        o[e] = activate_prescaled<T>(acc, use_silu);
-    }
-#pragma unroll
-    for (int k = 0; k + 1 < K; ++k) {
-        qh[k] = qh[k + 1];
-#pragma unroll
-        for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
-    }
-    if (K > 0) {
-        qh[K - 1] = q;
-#pragma unroll
-        for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
-    }
-}
-
+// Channel-last: blockIdx.x is a 64-thread channel block, blockIdx.y one of gridDim.y equal shares
+// of the flattened (batch, token) rows (as fwd_channel_last_share_kernel). A thread walks its
+// 16-byte channel group through the share: the history of each batch stretch comes from x, or
+// from the initial states before token 0; the stretch that ends a row writes its final states.
 template <typename T, int W, bool SEQ>
 __global__ void __launch_bounds__(kStThreads)
-    fwd_states_vec_kernel(const FwdStateArgs a, int64_t nstrips, bool wvec, bool bvec) {
+    fwd_states_vec_kernel(const FwdStateArgs a, bool wvec, bool bvec) {
     constexpr int V = Vec<T>::V;
     const FwdArgs& f = a.f;
     const int64_t nvec = f.D / V;
@@ -132,38 +102,31 @@ __global__ void __launch_bounds__(kStThreads)
                       w, bv);
     const bool use_silu = f.silu != 0;
     prescale_filter<T, W>(w, bv, use_silu);
-    const int64_t units = nstrips * f.B;
-    for (int64_t u = blockIdx.y; u < units; u += gridDim.y) {
-        const int64_t b = u / nstrips;
-        const int64_t t0 = (u - b * nstrips) * kStStrip;
-        const int64_t t1 = min(t0 + kStStrip, f.L);
+    const int64_t total = f.B * f.L;
+    int64_t r = total * blockIdx.y / gridDim.y;
+    const int64_t end = total * (blockIdx.y + 1) / gridDim.y;
+    if (f.L == 0) {
+        // Nothing to convolve: the final states are the tails of the initial states.
+        for (int64_t b = blockIdx.y; b < f.B; b += gridDim.y)
+            if (a.fin != nullptr) states_final<T, W>(a, b, c0, V);
+        return;
+    }
+    while (r < end) {
+        const int64_t b = r / f.L;
+        const int64_t t0 = r - b * f.L;
+        const int64_t n = min(end - r, f.L - t0);
         const T* xb = (const T*)f.x + b * f.x_sb + c0;
         T* ob = (T*)f.out + b * f.o_sb + c0;
-        const int32_t* qb = SEQ ? a.seq + b * a.q_sb : nullptr;
         float h[W - 1][V];
-        int32_t qh[W > 1 ? W - 1 : 1];
+        int32_t qh[W - 1];
         states_halo<T, W>(a, b, c0, t0, h, qh);
-        for (int64_t t = t0; t < t1; t += kStRows) {
-            uint4 r[kStRows];
-            int32_t q[kStRows];
-#pragma unroll
-            for (int i = 0; i < kStRows; ++i) {
-                if (t + i < t1) {
-                    r[i] = ldg16_stream(xb + (t + i) * f.x_sl);
-                    q[i] = SEQ ? __ldg(qb + (t + i) * a.q_sl) : 0;
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kStRows; ++i) {
-                if (t + i < t1) {
-                    float xv[V], o[V];
-                    unpack16<T>(r[i], xv);
-                    states_step<T, W, SEQ>(h, qh, xv, q[i], w, bv, use_silu, o);
-                    st16_stream(ob + (t + i) * f.o_sl, pack16<T>(o));
-                }
-            }
-        }
-        if (a.fin != nullptr && t1 == f.L) states_final<T, W>(a, b, c0, V);
+        if (SEQ)
+            walk_strip_seq<T, W, kStRows>(xb, f.x_sl, ob, f.o_sl, a.seq + b * a.q_sb, a.q_sl, t0,
+                                          t0 + n, h, qh, w, bv, use_silu);
+        else
+            walk_strip<T, W, kStRows, true>(xb, f.x_sl, ob, f.o_sl, t0, t0 + n, h, w, bv, use_silu);
+        if (a.fin != nullptr && t0 + n == f.L) states_final<T, W>(a, b, c0, V);
+        r += n;
     }
 }
 
@@ -245,12 +208,22 @@ cudaError_t run_fwd_states(const FwdStateArgs& a, cudaStream_t stream) {
                     host_aligned16(f.out) && (f.x_sl * e) % 16 == 0 && (f.o_sl * e) % 16 == 0 &&
                     (f.x_sb * e) % 16 == 0 && (f.o_sb * e) % 16 == 0;
     if (cl) {
-        dim3 grid((unsigned)ceil_div(f.D / V, (int64_t)kStThreads),
-                  (unsigned)std::min<int64_t>(nstrips * f.B, 65535));
-        if (a.seq != nullptr)
-            fwd_states_vec_kernel<T, W, true><<<grid, kStThreads, 0, stream>>>(a, nstrips, wvec, bvec);
-        else
-            fwd_states_vec_kernel<T, W, false><<<grid, kStThreads, 0, stream>>>(a, nstrips, wvec, bvec);
+        // Launch table as for the plain channel-last prefill (fwd.cu): many ~128-row shares,
+        // balanced by the block scheduler, for W <= 3 or short sequences when they give at least
+        // half a wave of CTAs; otherwise one balanced wave.
+        const int64_t gx = ceil_div(f.D / V, (int64_t)kStThreads);
+        static int slot_cache[2][kSlotCacheDevices] = {};
+        const bool seq = a.seq != nullptr;
+        auto kern = seq ? fwd_states_vec_kernel<T, W, true> : fwd_states_vec_kernel<T, W, false>;
+        const int64_t slots = device_slots((const void*)kern, kStThreads, slot_cache[seq]);
+        const int64_t rows = std::max<int64_t>(f.B * f.L, 1);
+        const int64_t strips = ceil_div(rows, kStStrip);
+        int64_t gy = (W <= 3 || f.L <= kStStrip) && strips * gx * 2 >= slots
+                         ? strips
+                         : std::min<int64_t>(std::max<int64_t>(slots, 1) / gx, ceil_div(rows, (int64_t)16));
+        if (f.L == 0) gy = f.B;
+        gy = std::max<int64_t>(1, std::min<int64_t>(gy, 65535));
+        kern<<<dim3((unsigned)gx, (unsigned)gy), kStThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     const int64_t n = f.B * f.D * nstrips;

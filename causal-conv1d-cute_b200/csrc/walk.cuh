@@ -117,6 +117,87 @@ __device__ __forceinline__ void walk_strip(const T* __restrict__ xb, int64_t x_s
     for (; t < tb; ++t) emit(ldg16_stream(xb + t * x_st), t);
 }
 
+// conv_step with per-token sequence ids: a history tap counts only when its id equals the
+// token's id q (a differing id adds nothing; the term is skipped, not multiplied by zero). The
+// window ids qh shift with the values.
+template <typename T, int W>
+__device__ __forceinline__ void conv_step_seq(float (&h)[W - 1][Vec<T>::V], int32_t (&qh)[W - 1],
+                                              const float* xv, int32_t q,
+                                              const float (&w)[W][Vec<T>::V],
+                                              const float (&bv)[Vec<T>::V], bool use_silu,
+                                              float* o) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+        float acc = bv[e];
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = qh[k] == q ? fmaf(h[k][e], w[k][e], acc) : acc;
+        acc = fmaf(xv[e], w[K][e], acc);
+        o[e] = activate_prescaled<T>(acc, use_silu);
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k) {
+        qh[k] = qh[k + 1];
+#pragma unroll
+        for (int e = 0; e < V; ++e) h[k][e] = h[k + 1][e];
+    }
+    qh[K - 1] = q;
+#pragma unroll
+    for (int e = 0; e < V; ++e) h[K - 1][e] = xv[e];
+}
+
+// walk_strip (with prefetch) for rows carrying sequence ids qb[row * q_st].
+template <typename T, int W, int U>
+__device__ __forceinline__ void walk_strip_seq(const T* __restrict__ xb, int64_t x_st,
+                                               T* __restrict__ ob, int64_t o_st,
+                                               const int32_t* __restrict__ qb, int64_t q_st,
+                                               int64_t ta, int64_t tb,
+                                               float (&h)[W - 1][Vec<T>::V], int32_t (&qh)[W - 1],
+                                               const float (&w)[W][Vec<T>::V],
+                                               const float (&bv)[Vec<T>::V], bool use_silu) {
+    constexpr int V = Vec<T>::V;
+    int64_t t = ta;
+    auto emit = [&](const uint4& r, int32_t q, int64_t row) {
+        float xv[V], o[V];
+        unpack16<T>(r, xv);
+        conv_step_seq<T, W>(h, qh, xv, q, w, bv, use_silu, o);
+        st16_stream(ob + row * o_st, pack16<T>(o));
+    };
+    uint4 nxt[U];
+    int32_t nq[U];
+    bool have = t + U <= tb;
+    if (have) {
+#pragma unroll
+        for (int i = 0; i < U; ++i) {
+            nxt[i] = ldg16_stream(xb + (t + i) * x_st);
+            nq[i] = __ldg(qb + (t + i) * q_st);
+        }
+    }
+    while (have) {
+        uint4 cur[U];
+        int32_t cq[U];
+#pragma unroll
+        for (int i = 0; i < U; ++i) {
+            cur[i] = nxt[i];
+            cq[i] = nq[i];
+        }
+        const int64_t tn = t + U;
+        have = tn + U <= tb;
+        if (have) {
+#pragma unroll
+            for (int i = 0; i < U; ++i) {
+                nxt[i] = ldg16_stream(xb + (tn + i) * x_st);
+                nq[i] = __ldg(qb + (tn + i) * q_st);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < U; ++i) emit(cur[i], cq[i], t + i);
+        t = tn;
+    }
+    for (; t < tb; ++t) emit(ldg16_stream(xb + t * x_st), __ldg(qb + t * q_st), t);
+}
+
 // Window of the W-1 rows before t0 (zeros before the sequence start).
 template <typename T, int W>
 __device__ __forceinline__ void load_halo(const T* xb, int64_t x_st, int64_t t0,
