@@ -18,7 +18,8 @@ all-gather a sample of every rank's outputs and compare them bit for bit with th
 
 With N = 1 the other BASELINE paths are measured too ("paths"): config 2 stored channel-first,
 config 2 with initial and final states and with sequence ids (the Dao-interface extras), indexed
-decode (config 3) and its ring variant, the 4-step speculative verify with dense per-step states
+decode (config 3) and its ring variant with the to_ring / from_ring conversions, the 4-step
+speculative verify with dense per-step states
 (config 4), and packed varlen prefill (config 5) at widths 2, 3, 4 and 8, each replayed in a CUDA
 graph (no host launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
 exceeds L2, and "warm" repeats one set.
@@ -377,6 +378,19 @@ def run_paths(device, reps=50, sets=8):
         calls.append(lambda x=x, ring=ring, seen=seen: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen))
     nbytes = 2 * Bd * D * 2 + 3 * Bd * D * 2 + Bd * D * 2 + D * 4 * 2 + D * 2 + Bd * 4
     record("decode_ring_b256", calls, nbytes)
+
+    # Ring layout conversions at the config-3 ring shape (the state a prefill hands to ring
+    # decode, and back): read and write 256 x 8192 x 3 elements each.
+    to_calls, from_calls = [], []
+    for _ in range(sets):
+        st = torch.randn(Bd, D, 3, device=device, generator=g).to(bf)
+        ring = torch.randn(Bd, 3, D, device=device, generator=g).to(bf)
+        seen = torch.randint(1, 8193, (Bd,), device=device, generator=g, dtype=torch.int32)
+        to_calls.append(lambda st=st, seen=seen: C.to_ring(st, seen))
+        from_calls.append(lambda ring=ring, seen=seen: C.from_ring(ring, seen))
+    nbytes = 2 * Bd * D * 3 * 2 + Bd * 4
+    record("to_ring_b256", to_calls, nbytes)
+    record("from_ring_b256", from_calls, nbytes)
 
     # Config 4: spec-decode verify, B=64, 4 steps, dense per-step states.
     Bs, S = 64, 4

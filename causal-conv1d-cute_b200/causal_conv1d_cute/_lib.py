@@ -33,6 +33,8 @@ SIGNATURES = {
                     _p, _i64, _i64, _i32, _i32, _i32, _i32, _p, _p],
     "cc1d_update_ring": [_p, _i64, _i64, _p, _i64, _i64, _i64, _i64, _p, _i64, _i64, _p, _i64,
                          _p, _i64, _i64, _p, _p, _i32, _i64, _i64, _i32, _i32, _i32, _p, _p],
+    "cc1d_to_ring": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p],
+    "cc1d_from_ring": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _i64, _i64, _i32, _i32, _p],
     "cc1d_varlen": [_p, _i64, _i64, _p, _i64, _i64, _p, _i64, _p, _i64, _i64, _p, _i64, _i64,
                     _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _p, _p],
     "cc1d_update_unpack": [_p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i32,

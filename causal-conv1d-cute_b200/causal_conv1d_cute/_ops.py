@@ -149,6 +149,18 @@ def update_ring(x, ring, weight, bias, silu, out, seen, idx, pad):
     return out
 
 
+def ring_convert(to_ring, state, ring, seen):
+    """Ordered state (slots, dim, W-1) <-> ring state (slots, W-1, dim) (cc1d_to_ring /
+    cc1d_from_ring); seen is an int32 CUDA tensor (slots,)."""
+    lib = load()
+    S, D, K = state.shape
+    args = (state.data_ptr(), *state.stride(), ring.data_ptr(), *ring.stride())
+    if not to_ring:
+        args = (ring.data_ptr(), *ring.stride(), state.data_ptr(), *state.stride())
+    f = lib.cc1d_to_ring if to_ring else lib.cc1d_from_ring
+    check(f(*args, seen.data_ptr(), S, D, K + 1, dtype_code(state.dtype), _stream(state.device)))
+
+
 def varlen(x, weight, bias, silu, out, qsl, cidx, hinit, states, pad):
     """Packed prefill of x (dim, ntokens) into out (dim, ntokens) (cc1d_varlen).
 
@@ -195,6 +207,6 @@ def update_unpack(qkvz, ba, state, weight, bias, out, z, b, a, idx, heads, silu,
 
 
 __all__ = [
-    "device_status", "fwd", "fwd_states", "set_device_checks", "update", "update_ring", "update_unpack",
+    "device_status", "fwd", "fwd_states", "ring_convert", "set_device_checks", "update", "update_ring", "update_unpack",
     "varlen", "_lib",
 ]

@@ -145,6 +145,54 @@ cc1d_status_t cc1d_fwd_states(const void* x, int64_t x_sb, int64_t x_sd, int64_t
                      "cc1d_fwd_states");
 }
 
+}  // extern "C"
+
+namespace {
+
+cc1d_status_t ring_convert(bool to_ring, const void* state, int64_t s_slot, int64_t s_sd,
+                           int64_t s_sk, const void* ring, int64_t r_slot, int64_t r_sk,
+                           int64_t r_sd, const int32_t* cache_seqlens, int64_t slots, int64_t dim,
+                           int32_t width, int32_t dtype, void* stream, const char* what) {
+    if (cc1d_status_t s = check_common(width, dtype)) return s;
+    if (slots < 0 || dim < 0)
+        return fail(CC1D_ERR_INVALID, "negative size (slots %lld, dim %lld)", (long long)slots,
+                    (long long)dim);
+    if (slots == 0 || dim == 0) return ok();
+    if (state == nullptr || ring == nullptr || cache_seqlens == nullptr)
+        return fail(CC1D_ERR_INVALID, "state, ring and cache_seqlens must not be NULL");
+    if (s_slot < 0 || s_sd < 0 || s_sk < 0 || r_slot < 0 || r_sk < 0 || r_sd < 0)
+        return fail(CC1D_ERR_LAYOUT, "strides must not be negative");
+    const int64_t e = dtype == CC1D_F32 ? 4 : 2;
+    const int64_t K = width - 1;
+    if (overlap(state, span_bytes(slots, s_slot, dim, s_sd, K, s_sk, e), ring,
+                span_bytes(slots, r_slot, K, r_sk, dim, r_sd, e)))
+        return fail(CC1D_ERR_INVALID, "the ring and the ordered state overlap");
+    cc1d::RingConvArgs a{state, s_slot, s_sd, s_sk, const_cast<void*>(ring), r_slot, r_sk, r_sd,
+                         cache_seqlens, slots, dim, to_ring};
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_ring_convert(a, width, dtype, (cudaStream_t)stream), what);
+}
+
+}  // namespace
+
+extern "C" {
+
+cc1d_status_t cc1d_to_ring(const void* state, int64_t s_slot, int64_t s_sd, int64_t s_sk,
+                           void* ring, int64_t r_slot, int64_t r_sk, int64_t r_sd,
+                           const int32_t* cache_seqlens, int64_t slots, int64_t dim,
+                           int32_t width, int32_t dtype, void* stream) {
+    return ring_convert(true, state, s_slot, s_sd, s_sk, ring, r_slot, r_sk, r_sd, cache_seqlens,
+                        slots, dim, width, dtype, stream, "cc1d_to_ring");
+}
+
+cc1d_status_t cc1d_from_ring(const void* ring, int64_t r_slot, int64_t r_sk, int64_t r_sd,
+                             void* state, int64_t s_slot, int64_t s_sd, int64_t s_sk,
+                             const int32_t* cache_seqlens, int64_t slots, int64_t dim,
+                             int32_t width, int32_t dtype, void* stream) {
+    return ring_convert(false, state, s_slot, s_sd, s_sk, ring, r_slot, r_sk, r_sd, cache_seqlens,
+                        slots, dim, width, dtype, stream, "cc1d_from_ring");
+}
+
 cc1d_status_t cc1d_update(const void* x, int64_t x_sb, int64_t x_sd, int64_t x_st,
                           void* state, int64_t s_slot, int64_t s_sd, int64_t s_sk,
                           int64_t state_len, int64_t nslots,

@@ -75,6 +75,18 @@ struct RingArgs {
     int32_t* status;
 };
 
+// Conversion between the ordered conv state (slots, dim, W-1) and the ring state
+// (slots, W-1, dim): ring row (seen[s] + k) % (W-1) holds ordered entry k.
+struct RingConvArgs {
+    const void* state;
+    int64_t s_slot, s_sd, s_sk;
+    void* ring;
+    int64_t r_slot, r_sk, r_sd;
+    const int32_t* seen;
+    int64_t S, D;
+    bool to_ring;  // state -> ring; otherwise ring -> state
+};
+
 struct VarArgs {
     const void* x;
     int64_t x_sd, x_st;
@@ -120,6 +132,7 @@ cudaError_t launch_fwd(const FwdArgs& a, int width, int dtype, cudaStream_t stre
 cudaError_t launch_fwd_states(const FwdStateArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_update(const UpdArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_ring(const RingArgs& a, int width, int dtype, cudaStream_t stream);
+cudaError_t launch_ring_convert(const RingConvArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_varlen(const VarArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_unpack(const UnpackArgs& a, int width, int dtype, cudaStream_t stream);
 

@@ -7,6 +7,10 @@
 // tap k (oldest first) takes row (pos + k) % (W-1), picked from registers by a select chain so
 // that the weight loads never wait on the sequence length. The taps are summed oldest first, the
 // order of the ordered-state decode, so both layouts give identical outputs.
+//
+// to_ring / from_ring (ring.py:33-67) run here too: a thread moves one 16-byte channel vector of
+// one slot between the channel-major state block (W-1 vectors, transposed in registers) and the
+// W-1 ring rows, rotated by the slot's sequence length.
 #include <algorithm>
 
 #include "common.cuh"
@@ -132,11 +136,96 @@ cudaError_t run_ring(const RingArgs& a, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+// Ordered state <-> ring state, one 16-byte channel vector of one slot (blockIdx.y) per thread.
+template <typename T, int W, bool TO_RING>
+__global__ void __launch_bounds__(kRingThreads) ring_convert_kernel(const RingConvArgs a) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    const int64_t j = (int64_t)blockIdx.x * kRingThreads + threadIdx.x;
+    if (j >= a.D / V) return;
+    const int64_t c0 = j * V;
+    const int64_t s = blockIdx.y;
+    const int pos = ring_pos(__ldg(a.seen + s), K);
+    T* sp = (T*)a.state + s * a.s_slot + c0 * K;
+    T* rp = (T*)a.ring + s * a.r_slot + c0;
+    uint4 blk[K], tm[K];
+    if (TO_RING) {
+#pragma unroll
+        for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
+        block_to_time<T, K>(blk, tm);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int r = pos + k >= K ? pos + k - K : pos + k;
+            st16(rp + r * a.r_sk, tm[k]);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const int r = pos + k >= K ? pos + k - K : pos + k;
+            tm[k] = ld16(rp + r * a.r_sk);
+        }
+        time_to_block<T, K>(tm, blk);
+#pragma unroll
+        for (int q = 0; q < K; ++q) st16(sp + q * V, blk[q]);
+    }
+}
+
+// Any strides: one element per thread.
+template <typename T, int W>
+__global__ void __launch_bounds__(kGenThreads) ring_convert_generic_kernel(const RingConvArgs a) {
+    constexpr int K = W - 1;
+    const int64_t n = a.S * a.D * K;
+    for (int64_t id = (int64_t)blockIdx.x * kGenThreads + threadIdx.x; id < n;
+         id += (int64_t)gridDim.x * kGenThreads) {
+        const int k = (int)(id % K);
+        const int64_t c = (id / K) % a.D;
+        const int64_t s = id / (K * a.D);
+        const int p = ring_pos(a.seen[s], K) + k;
+        const int r = p >= K ? p - K : p;
+        T* se = (T*)a.state + s * a.s_slot + c * a.s_sd + k * a.s_sk;
+        T* re = (T*)a.ring + s * a.r_slot + r * a.r_sk + c * a.r_sd;
+        if (a.to_ring)
+            *re = *se;
+        else
+            *se = *re;
+    }
+}
+
+template <typename T, int W>
+cudaError_t run_ring_convert(const RingConvArgs& a, cudaStream_t stream) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    const int64_t e = sizeof(T);
+    const bool vec = a.D % V == 0 && a.s_sk == 1 && a.s_sd == K && a.r_sd == 1 &&
+                     host_aligned16(a.state) && host_aligned16(a.ring) &&
+                     (a.s_slot * e) % 16 == 0 && (a.r_slot * e) % 16 == 0 &&
+                     (a.r_sk * e) % 16 == 0 && a.S <= 65535;
+    if (vec) {
+        dim3 grid((unsigned)ceil_div(a.D / V, (int64_t)kRingThreads), (unsigned)a.S);
+        if (a.to_ring)
+            ring_convert_kernel<T, W, true><<<grid, kRingThreads, 0, stream>>>(a);
+        else
+            ring_convert_kernel<T, W, false><<<grid, kRingThreads, 0, stream>>>(a);
+        return cudaGetLastError();
+    }
+    const int64_t n = a.S * a.D * K;
+    const int64_t blocks = std::max<int64_t>(1, std::min<int64_t>(ceil_div(n, kGenThreads), 148 * 32));
+    ring_convert_generic_kernel<T, W><<<(unsigned)blocks, kGenThreads, 0, stream>>>(a);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_ring(const RingArgs& a, int width, int dtype, cudaStream_t stream) {
     cudaError_t err = cudaErrorInvalidValue;
     CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_ring<T, kW>(a, stream))));
+    return err;
+}
+
+cudaError_t launch_ring_convert(const RingConvArgs& a, int width, int dtype, cudaStream_t stream) {
+    cudaError_t err = cudaErrorInvalidValue;
+    CC1D_DISPATCH_DTYPE(dtype,
+                        CC1D_DISPATCH_WIDTH(width, err = (run_ring_convert<T, kW>(a, stream))));
     return err;
 }
 

@@ -25,32 +25,6 @@ constexpr int kGenThreads = 256;
 
 enum { kInterNone = 0, kInterDense = 1, kInterDedup = 2 };
 
-// Transpose between the channel-major state block (element e*SS + s of the block, V*SS
-// elements in SS vectors) and SS time-major vectors (vector s, lane e).
-template <typename T, int SS>
-__device__ __forceinline__ void block_to_time(const uint4 (&blk)[SS], uint4 (&tm)[SS]) {
-    constexpr int V = Vec<T>::V;
-#pragma unroll
-    for (int e = 0; e < V; ++e)
-#pragma unroll
-        for (int s = 0; s < SS; ++s) {
-            const int flat = e * SS + s;
-            set_lane<T>(tm[s], e, lane_of<T>(blk[flat / V], flat % V));
-        }
-}
-
-template <typename T, int N>
-__device__ __forceinline__ void time_to_block(const uint4* tm, uint4 (&blk)[N]) {
-    constexpr int V = Vec<T>::V;
-#pragma unroll
-    for (int q = 0; q < N; ++q)
-#pragma unroll
-        for (int i = 0; i < V; ++i) {
-            const int flat = q * V + i;
-            set_lane<T>(blk[q], i, lane_of<T>(tm[flat % N], flat / N));
-        }
-}
-
 // One batch row of one channel group, with its x rows (xr) and state block (sr) already loaded.
 template <typename T, int W, int SS, int LMAX, int IMODE>
 __device__ __forceinline__ void update_row(const UpdArgs& a, const uint4 (&wt)[W], const uint4& bt,

@@ -146,6 +146,22 @@ cc1d_status_t cc1d_update_ring(const void* x, int64_t x_sb, int64_t x_sd,
                                int32_t dtype, int32_t silu, int32_t* dev_status, void* stream);
 
 /*
+ * Layout conversion between the ordered conv state (slots, dim, W-1) (the prefill / decode
+ * layout, oldest entry first) and the ring state (slots, W-1, dim) of cc1d_update_ring: ring row
+ * (cache_seqlens[s] + k) mod (W-1) of slot s holds ordered entry k. width is W (2..8); the two
+ * tensors, given by element strides, must not overlap.
+ * Replaces: to_ring / from_ring (ring.py:33-67), torch gathers in the reference.
+ */
+cc1d_status_t cc1d_to_ring(const void* state, int64_t s_slot, int64_t s_sd, int64_t s_sk,
+                           void* ring, int64_t r_slot, int64_t r_sk, int64_t r_sd,
+                           const int32_t* cache_seqlens, int64_t slots, int64_t dim,
+                           int32_t width, int32_t dtype, void* stream);
+cc1d_status_t cc1d_from_ring(const void* ring, int64_t r_slot, int64_t r_sk, int64_t r_sd,
+                             void* state, int64_t s_slot, int64_t s_sd, int64_t s_sk,
+                             const int32_t* cache_seqlens, int64_t slots, int64_t dim,
+                             int32_t width, int32_t dtype, void* stream);
+
+/*
  * Packed variable-length prefill. x and out are (dim, ntokens). Token-major views (x_sd == 1,
  * the serving layout) take ONE vectorised launch for any number of sequences; contiguous
  * channel-first storage (x_st == 1) takes a vectorised stream pass plus a per-(channel, sequence)

@@ -14,13 +14,13 @@ from causal_conv1d_cute import causal_conv1d_update, causal_conv1d_update_ring, 
 PAD = -1
 
 
-def test_round_trip_between_layouts_cpu():
-    torch.manual_seed(0)
-    st = torch.randn(7, 32, 3)
-    n = torch.randint(0, 50, (7,), dtype=torch.int32)
-    ring = to_ring(st, n)
-    assert ring.shape == (7, 3, 32) and torch.equal(from_ring(ring, n), st)
-    assert np.array_equal(ring.numpy(), oracle.to_ring(st.numpy(), n.numpy()))
+def test_layout_conversion_has_no_cpu_path():
+    from causal_conv1d_cute import Unsupported
+
+    with pytest.raises(Unsupported):
+        to_ring(torch.randn(7, 32, 3), torch.zeros(7, dtype=torch.int32))
+    with pytest.raises(ValueError):
+        to_ring(torch.randn(7, 32), torch.zeros(7, dtype=torch.int32))
 
 
 @pytest.mark.gpu
@@ -30,6 +30,29 @@ def test_round_trip_between_layouts():
     n = torch.randint(0, 50, (7,), device="cuda", dtype=torch.int32)
     ring = to_ring(st, n)
     assert ring.shape == (7, 3, 32) and torch.equal(from_ring(ring, n), st)
+    assert np.array_equal(ring.cpu().numpy(), oracle.to_ring(st.cpu().numpy(), n.cpu().numpy()))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("K", [1, 2, 3, 7])
+@pytest.mark.parametrize("layout", ["contiguous", "strided"])
+def test_conversion_kernels_match_oracle(K, dtype, layout):
+    """Vector kernel (contiguous, 16-byte aligned) and element kernel (strided views, odd dim),
+    negative and large sequence lengths, int64 lengths."""
+    torch.manual_seed(K)
+    S, D = 33, 1024 if layout == "contiguous" else 100
+    st = torch.randn(S, D, K, device="cuda").to(dtype)
+    if layout == "strided":
+        st = torch.randn(S, K, D + 3, device="cuda").to(dtype)[:, :, 1:D + 1].transpose(1, 2)
+    n = torch.randint(-1000, 10**6, (S,), device="cuda", dtype=torch.int64)
+    ring = to_ring(st, n)
+    exp = oracle.to_ring(to_np(st), n.cpu().numpy())
+    assert_bits(ring, exp)
+    back_src = ring if layout == "contiguous" else ring.transpose(1, 2).contiguous().transpose(1, 2)
+    back = from_ring(back_src, n)
+    assert_bits(back, to_np(st))
+    assert back.is_contiguous()
 
 
 @pytest.mark.gpu
