@@ -83,3 +83,13 @@ def test_host_validation_rejects_before_launch():
     # fused decode: dim not a multiple of the vector width
     uargs = [1, 0, 1, 0, 1, 0, 1, None, 1, 1, 1, 1, 1, -1, 1, 12, 16, 4, 4, 0, 0, 1, None]
     assert lib.cc1d_update_unpack(*uargs) == 4
+    # prefill with states: sequence ids exclude states
+    fargs = [1, 0, 0, 0, 1, 0, 0, None, 0, 1, 0, 0, 0, 1, 0, 0, 1, 0, 0, 0, None, 0, 0, 0,
+             1, 16, 16, 4, 0, 0, None]
+    assert lib.cc1d_fwd_states(*fargs) == 1 and b"exclude" in lib.cc1d_last_error()
+    # ring conversion: state and ring overlap
+    rargs = [4096, 48, 3, 1, 4096, 48, 16, 1, 8, 1, 16, 4, 0, None]
+    assert lib.cc1d_to_ring(*rargs) == 1 and b"overlap" in lib.cc1d_last_error()
+    # ring conversion: width outside 2..8
+    rargs[11] = 9
+    assert lib.cc1d_from_ring(*rargs) == 3
