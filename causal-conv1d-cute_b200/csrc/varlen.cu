@@ -613,7 +613,12 @@ cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
     if (cf) {
         const int64_t total = a.D * a.T;
         const int64_t chunks = ceil_div(total, 32 * kCfElems);
-        const int iters = (int)std::max<int64_t>(1, std::min<int64_t>(8, chunks / (148 * 64)));
+        // One wave of warps, each walking an equal run of chunks (as the channel-first prefill).
+        static int slot_cache[kSlotCacheDevices] = {};
+        const int64_t wave_warps =
+            std::max<int64_t>(1, device_slots((const void*)varlen_channel_first_kernel<T, W>,
+                                              kCfThreads, slot_cache)) * (kCfThreads / 32);
+        const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
         const int64_t warps = ceil_div(chunks, iters);
         varlen_channel_first_kernel<T, W>
             <<<(unsigned)ceil_div(warps * 32, kCfThreads), kCfThreads, 0, stream>>>(a, total, iters);
