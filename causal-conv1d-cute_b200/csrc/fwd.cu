@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(NT, MINB)
 // from the lane to its left by a warp shuffle; lane 0 gets them from lane 31 of the previous
 // iteration, so every element is read from HBM once. The next iteration's vectors are requested
 // before the current ones are computed. A lane's elements straddle at most one row boundary.
-template <typename T, int W>
+template <typename T, int W, bool V32>
 __global__ void __launch_bounds__(kCfThreads)
     fwd_channel_first_kernel(const FwdArgs a, int64_t total, int iters) {
     constexpr int K = W - 1;
@@ -127,8 +127,13 @@ __global__ void __launch_bounds__(kCfThreads)
     }
     auto load = [&](int64_t g, uint4 (&v)[NV]) {
         if (g + EPT <= total) {
+            if (V32) {
 #pragma unroll
-            for (int q = 0; q < NV; ++q) v[q] = ldg16_stream(x + g + q * PER);
+                for (int q = 0; q < NV; q += 2) ldg32_stream(x + g + q * PER, v[q], v[q + 1]);
+            } else {
+#pragma unroll
+                for (int q = 0; q < NV; ++q) v[q] = ldg16_stream(x + g + q * PER);
+            }
         } else {
 #pragma unroll
             for (int q = 0; q < NV; ++q) {
@@ -176,8 +181,16 @@ __global__ void __launch_bounds__(kCfThreads)
                     for (int k = 0; k < W; ++k) acc = fmaf(win[e + k], w0[k], acc);
                     o[e] = activate<T>(acc, use_silu);
                 }
+                if (V32) {
 #pragma unroll
-                for (int q = 0; q < NV; ++q) st16_stream(out + f + q * PER, pack16<T>(o + q * PER));
+                    for (int q = 0; q < NV; q += 2)
+                        st32_stream(out + f + q * PER, pack16<T>(o + q * PER),
+                                    pack16<T>(o + (q + 1) * PER));
+                } else {
+#pragma unroll
+                    for (int q = 0; q < NV; ++q)
+                        st16_stream(out + f + q * PER, pack16<T>(o + q * PER));
+                }
             } else {
                 float w1[W], b1 = 0.f;
                 const bool straddle = t + EPT > L;
@@ -332,14 +345,17 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
         const int64_t chunks = ceil_div(total, 32 * kCfElems);  // one warp iteration each
         // One wave: every resident warp walks an equal run of chunks (measured on B200 at the
         // config-2 sizes: 8 chunks per warp 196.5 us, 16: 189.8, 32: 188.1, one wave: 187.4).
-        static int slot_cache[kSlotCacheDevices] = {};
+        // 32-byte accesses when both streams are 32-byte aligned (a lane's 16 elements are).
+        const bool v32 = host_aligned32(a.x) && host_aligned32(a.out);
+        auto kern = v32 ? fwd_channel_first_kernel<T, W, true> : fwd_channel_first_kernel<T, W, false>;
+        static int slot_cache[2][kSlotCacheDevices] = {};
         const int64_t wave_warps =
-            std::max<int64_t>(1, device_slots((const void*)fwd_channel_first_kernel<T, W>,
-                                              kCfThreads, slot_cache)) * (kCfThreads / 32);
+            std::max<int64_t>(1, device_slots((const void*)kern, kCfThreads, slot_cache[v32])) *
+            (kCfThreads / 32);
         const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
         const int64_t warps = ceil_div(chunks, iters);
         const int64_t blocks = ceil_div(warps * 32, kCfThreads);
-        fwd_channel_first_kernel<T, W><<<(unsigned)blocks, kCfThreads, 0, stream>>>(a, total, iters);
+        kern<<<(unsigned)blocks, kCfThreads, 0, stream>>>(a, total, iters);
         return cudaGetLastError();
     }
     const int strip = 64;
