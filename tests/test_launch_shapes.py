@@ -99,3 +99,23 @@ def test_varlen_launch_forms_match_scalar_path(case):
         mask = ~np.isnan(r_out)
         assert_close(to_np(y), np.nan_to_num(r_out), torch.bfloat16, mask)
         assert_bits(st, r_st)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_channel_first_prefill_16_byte_aligned_stream(dtype):
+    """Contiguous (B, D, L) storage starting 16 bytes past a 32-byte line takes the 16-byte access
+    variant of the flat-stream kernel; it must equal the 32-byte variant bit for bit."""
+    B, D, L, W = 2, 96, 1000, 4
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(B, D, L, device="cuda", generator=g).to(dtype)
+    w = (torch.rand(D, W, device="cuda", generator=g) - 0.5).to(dtype)
+    off = 16 // x.element_size()
+    buf = torch.empty(B * D * L + off, device="cuda", dtype=dtype)
+    xs = buf[off:].view(B, D, L)
+    xs.copy_(x)
+    assert xs.data_ptr() % 32 == 16
+    y = causal_conv1d_fn(x, w, None, "silu")
+    ys = causal_conv1d_fn(xs, w, None, "silu")
+    torch.cuda.synchronize()
+    assert torch.equal(y, ys)
