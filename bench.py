@@ -23,7 +23,8 @@ With N = 1 the other BASELINE paths are measured too ("paths"): config 2 stored 
 config 2 with initial and final states and with sequence ids (the Dao-interface extras), indexed
 decode (config 3) and its ring variant with the to_ring / from_ring conversions, the 4-step
 speculative verify with dense per-step states
-(config 4), and packed varlen prefill (config 5) at widths 2, 3, 4 and 8, each replayed in a CUDA
+(config 4), and packed varlen prefill (config 5) at widths 2, 3, 4 and 8, token-major and
+channel-first, each replayed in a CUDA
 graph (no host launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
 exceeds L2, and "warm" repeats one set.
 
@@ -430,7 +431,8 @@ def run_paths(device, reps=50, sets=8):
     nbytes = 2 * Bs * S * D * 2 + 2 * Bs * D * 3 * 2 + Bs * S * D * 3 * 2 + D * 4 * 2 + D * 2 + 2 * Bs * 4
     record("spec_decode_b64_s4", calls, nbytes)
 
-    # Config 5: varlen, 32 lognormal(7, 1) lengths clipped to [1, 8192], token-major x.
+    # Config 5: varlen, 32 lognormal(7, 1) lengths clipped to [1, 8192], token-major x, and the
+    # same batch stored channel-first.
     rng = np.random.default_rng(0)
     lens = np.clip(np.round(rng.lognormal(7, 1, 32)), 1, 8192).astype(np.int64)
     T = int(lens.sum())
@@ -438,6 +440,7 @@ def run_paths(device, reps=50, sets=8):
     cidx = torch.from_numpy(rng.choice(512, 32, replace=False).astype(np.int32)).to(device)
     hinit = torch.from_numpy(rng.random(32) < 0.5).to(device)
     xv = torch.randn(T, D, device=device, generator=g).to(bf)
+    xc = xv.t().contiguous()
     for Wv in (2, 3, 4, 8):
         wv = (torch.rand(D, Wv, device=device, generator=g) - 0.5).to(bf)
         states = torch.randn(512, D, Wv - 1, device=device, generator=g).to(bf)
@@ -446,14 +449,12 @@ def run_paths(device, reps=50, sets=8):
         f = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xv.t(), wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
         us = graph_us([f], 20)
         res[f"varlen_w{Wv}"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3), "tokens": T}
-        if Wv == 4:
-            # The same batch stored channel-first: contiguous (8192, T).
-            xc = xv.t().contiguous()
-            fc = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xc, wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
-            us = graph_us([fc], 20)
-            res["varlen_w4_channel_first"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3),
-                                              "tokens": T}
-            del xc
+        # The same batch stored channel-first: contiguous (8192, T).
+        fc = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xc, wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
+        us = graph_us([fc], 20)
+        res[f"varlen_w{Wv}_channel_first"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3),
+                                             "tokens": T}
+    del xc
     return res
 
 

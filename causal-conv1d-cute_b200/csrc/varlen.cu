@@ -27,8 +27,6 @@ namespace cc1d {
 namespace {
 
 constexpr int kVarThreads = 64;
-constexpr int kCfThreads = 256;
-constexpr int kCfElems = 16;  // elements per lane per iteration of the channel-first stream pass
 constexpr int kBoundaryThreads = 128;
 constexpr int kGenThreads = 256;
 
@@ -197,267 +195,77 @@ __global__ void __launch_bounds__(NT, MINB)
 }
 
 // ---------------------------------------------------------------------------------------------
-// Channel-first: x is contiguous (D, T), one packed stream per channel. The D*T elements form one
-// flat stream; a lane owns 8 consecutive elements (one or two 16-byte vectors) and receives the
-// W-1 elements before them from the lane to its left (warp shuffle), so HBM is read once with
-// 16-byte coalesced loads whatever T is. Element f is token t = f % T of channel c = f / T.
-// Every (channel, sequence) pair has its own first token here, so the owner work is done by a
-// second, small launch with one thread per pair (varlen_boundary_kernel): done inside the stream
-// pass, each owner chain (slot -> state -> inputs) stalled its whole warp. The stream pass writes
-// only tokens at least W-1 past their sequence start and never touches the cache.
+// Channel-first: x is contiguous (D, T), one packed stream per channel. The bulk pass is the
+// channel-first prefill of a (1, D, T) batch (launch_fwd): it computes every output as if each
+// channel row were one sequence, so every output whose W-1 predecessors lie in its own sequence is
+// final. The others are the first W-1 outputs of each sequence, which a second, small launch with
+// one thread per (channel, sequence) pair (varlen_boundary_kernel) recomputes from the initial
+// state and overwrites, stream order placing it after the bulk pass; and outputs of tokens outside
+// every sequence, which are undefined. The boundary launch also reads and writes the cache, which
+// the bulk pass never touches. Tracking sequence bounds inside the stream pass instead cost a
+// quarter of its time at the config-5 shape: with 1.3k-token sequences, 40 % of the 512-token warp
+// steps meet a boundary and diverge into masked stores.
 // ---------------------------------------------------------------------------------------------
 
 // Owner work of sequence s in channel c of a contiguous (D, T) stream: initial state in, final
-// state out, and the first W-1 outputs, element by element.
+// state out, and the first W-1 outputs. Every load (inputs at both ends of the sequence, filter,
+// initial state) is issued before the first store, so a thread waits for memory once rather than
+// once per element (the compiler cannot move a load of x above a store to out by itself).
 template <typename T, int W>
 __device__ __forceinline__ void owner_channel(const VarArgs& a, int64_t c, int64_t s) {
     constexpr int K = W - 1;
     const int64_t bos = qsl_at(a, s);
     const int64_t eos = max(qsl_at(a, s + 1), bos);
+    const int64_t n = eos - bos;
     if (c == 0) check_bounds(a, s);
     const SeqSlot ss = seq_slot(a, s, c == 0);
-    T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c * a.s_sd : nullptr;
     const T* xr = (const T*)a.x + c * a.T;
     T* orow = (T*)a.out + c * a.T;
-    float wf[W], bf;
-    load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c, wf, bf);
-    T init[K];
-    float h[K];
+    T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c * a.s_sd : nullptr;
+    T head[K], tail[K], init[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) {
+        head[k] = k < n ? __ldg(xr + bos + k) : from_f32<T>(0.f);
+        const int64_t pos = eos - K + k;
+        tail[k] = pos >= bos ? __ldg(xr + pos) : from_f32<T>(0.f);
         init[k] = ss.use_init ? sp[k * a.s_sk] : from_f32<T>(0.f);
-        h[k] = to_f32<T>(init[k]);
     }
-    if (ss.live) {
-        const int64_t n = eos - bos;
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const int64_t pos = eos - K + k;
-            T v;
-            if (pos >= bos) {
-                v = xr[pos];
-            } else {
-                const int64_t m = k + n;
-                v = init[0];
-#pragma unroll
-                for (int q = 1; q < K; ++q) v = (m == q) ? init[q] : v;
-            }
-            sp[k * a.s_sk] = v;
-        }
-    }
+    float wf[W], bf;
+    load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c, wf, bf);
     const bool use_silu = a.silu != 0;
-    const int64_t hend = min(eos, bos + K);
-    for (int64_t tt = bos; tt < hend; ++tt) {
-        const float xv = to_f32<T>(xr[tt]);
+    float h[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) h[k] = to_f32<T>(init[k]);
+#pragma unroll
+    for (int j = 0; j < K; ++j) {
+        const float xv = to_f32<T>(head[j]);
         float acc = bf;
 #pragma unroll
         for (int k = 0; k < K; ++k) acc = fmaf(h[k], wf[k], acc);
         acc = fmaf(xv, wf[K], acc);
-        orow[tt] = from_f32<T>(activate<T>(acc, use_silu));
+        if (j < n) orow[bos + j] = from_f32<T>(activate<T>(acc, use_silu));
 #pragma unroll
         for (int k = 0; k + 1 < K; ++k) h[k] = h[k + 1];
         h[K - 1] = xv;
     }
-}
-
-// Bits lo..hi-1 set (0 <= lo, hi <= 32; empty when hi <= lo).
-__device__ __forceinline__ unsigned bit_range(int lo, int hi) {
-    if (hi <= lo) return 0u;
-    const unsigned upto = hi >= 32 ? 0xffffffffu : ((1u << hi) - 1u);
-    return upto & ~((1u << lo) - 1u);
-}
-
-// Sequence containing token t: s (-1 before the first sequence, nseq after the last), its start
-// and the token at which the containing sequence changes.
-struct SeqCursor {
-    int64_t s, bos, next;
-};
-
-__device__ __forceinline__ SeqCursor locate(const VarArgs& a, int64_t t) {
-    SeqCursor r;
-    r.s = seq_of(a, t);
-    r.bos = (r.s >= 0 && r.s < a.nseq) ? qsl_at(a, r.s) : 0;
-    r.next = r.s < 0 ? qsl_at(a, 0) : (r.s < a.nseq ? max(qsl_at(a, r.s + 1), r.bos) : INT64_MAX);
-    return r;
-}
-
-// Move the cursor forward to token t (t never decreases within a channel row): walk the
-// sequence list (a lane moves a few hundred tokens per step, so it crosses at most a few
-// boundaries), falling back to a binary search when many sequences lie in between.
-__device__ __forceinline__ void advance(const VarArgs& a, SeqCursor& q, int64_t t) {
-    for (int step = 0; t >= q.next; ++step) {
-        if (step == 8) {
-            q = locate(a, t);
-            return;
-        }
-        ++q.s;
-        while (q.s < a.nseq && qsl_at(a, q.s + 1) <= q.next) ++q.s;
-        q.bos = q.next;
-        q.next = q.s < a.nseq ? qsl_at(a, q.s + 1) : INT64_MAX;
-        if (q.s >= a.nseq) return;
-    }
-}
-
-template <typename T, int W>
-__global__ void __launch_bounds__(kCfThreads)
-    varlen_channel_first_kernel(const VarArgs a, int64_t total, int iters) {
-    constexpr int K = W - 1;
-    constexpr int EPT = kCfElems;
-    constexpr int PER = 16 / (int)sizeof(T);
-    constexpr int NV = EPT / PER;
-    constexpr int WSPAN = 32 * EPT;
-    const unsigned FULL = 0xffffffffu;
-    const int lane = threadIdx.x & 31;
-    const int64_t gw = ((int64_t)blockIdx.x * kCfThreads + threadIdx.x) >> 5;
-    const int64_t base = gw * (int64_t)iters * WSPAN;
-    if (base >= total) return;  // warp-uniform
-    const T* x = (const T*)a.x;
-    T* out = (T*)a.out;
-    const int64_t Tn = a.T;
-    const int64_t nseq = a.nseq;
-    const bool use_silu = a.silu != 0;
-
-    float carry[K];
-#pragma unroll
-    for (int k = 0; k < K; ++k) {
-        const int64_t p = base - K + k;
-        carry[k] = (lane == 0 && p >= 0) ? to_f32<T>(x[p]) : 0.f;
-    }
-    auto load = [&](int64_t g, uint4 (&v)[NV]) {
-        if (g + EPT <= total) {
-#pragma unroll
-            for (int q = 0; q < NV; ++q) v[q] = ldg16_stream(x + g + q * PER);
-        } else {
-#pragma unroll
-            for (int q = 0; q < NV; ++q) {
-                v[q] = make_uint4(0, 0, 0, 0);
-#pragma unroll
-                for (int i = 0; i < PER; ++i)
-                    if (g + q * PER + i < total) set_lane<T>(v[q], i, x[g + q * PER + i]);
-            }
-        }
-    };
-    // Position of this lane's first element (advanced by one warp stride per iteration) and its
-    // sequence.
-    int64_t f = base + lane * EPT;
-    int64_t c = f / Tn;
-    int64_t t = f - c * Tn;
-    uint4 cur[NV];
-    load(f, cur);
-    SeqCursor q = locate(a, t);
-    int64_t wc = -1;
-    float wf[W], bf = 0.f;
-    for (int it = 0; it < iters; ++it) {
-        f = base + (int64_t)it * WSPAN + lane * EPT;
-        uint4 nxt[NV];
-        if (it + 1 < iters) load(f + WSPAN, nxt);
-        float xv[EPT];
-#pragma unroll
-        for (int qv = 0; qv < NV; ++qv) unpack16<T>(cur[qv], xv + qv * PER);
-        float win[K + EPT];
+    if (ss.live) {
+        // The last K inputs of [initial state | sequence]: entry k is x[eos - K + k] when that
+        // lies in the sequence, else initial-state entry k + n.
 #pragma unroll
         for (int k = 0; k < K; ++k) {
-            const float up = __shfl_up_sync(FULL, xv[EPT - K + k], 1);
-            const float last = __shfl_sync(FULL, xv[EPT - K + k], 31);
-            win[k] = lane == 0 ? carry[k] : up;
-            carry[k] = last;
+            T v = tail[k];
+            if (eos - K + k < bos) {
+                const int64_t m = k + n;
+#pragma unroll
+                for (int q = 0; q < K; ++q) v = (m == q) ? init[q] : v;
+            }
+            sp[k * a.s_sk] = v;
         }
-#pragma unroll
-        for (int e = 0; e < EPT; ++e) win[K + e] = xv[e];
-        const bool full = f + EPT <= total;
-        if (f < total) {
-            advance(a, q, t);
-            if (c != wc) {
-                load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c,
-                                   wf, bf);
-                wc = c;
-            }
-            // The chunk holds tokens of sequence q.s before q.next and, when it crosses q.next,
-            // of the next sequence s1 = q.s + 1, which starts at q.next. With at most that one
-            // boundary inside the chunk (the common case) every output is computed uniformly and
-            // a mask keeps those that are neither head tokens nor outside every sequence.
-            bool simple = full && t + EPT <= Tn;
-            int64_t e1 = INT64_MAX;
-            if (simple && t + EPT > q.next) {
-                const int64_t s1 = q.s + 1;
-                e1 = s1 < nseq ? qsl_at(a, s1 + 1) : q.next;
-                simple = s1 < nseq && e1 > q.next && t + EPT <= e1;
-            }
-            if (simple) {
-                // Kept elements: [e0, nb) of sequence q.s and [nb + K, EPT) of s1, where nb is
-                // the chunk index of the boundary q.next and e0 skips q.s's head tokens.
-                const bool in0 = q.s >= 0 && q.s < nseq;
-                const int nb = (int)min(q.next - t, (int64_t)EPT);
-                const int into = (int)min(t - q.bos, (int64_t)K);
-                const int e0 = in0 ? K - into : nb;
-                const unsigned mask = bit_range(e0, nb) | bit_range(min(nb + K, EPT), EPT);
-                float o[EPT];
-#pragma unroll
-                for (int e = 0; e < EPT; ++e) {
-                    float acc = bf;
-#pragma unroll
-                    for (int k = 0; k < W; ++k) acc = fmaf(win[e + k], wf[k], acc);
-                    o[e] = activate<T>(acc, use_silu);
-                }
-                if (mask == (1u << EPT) - 1) {
-#pragma unroll
-                    for (int qv = 0; qv < NV; ++qv)
-                        st16_stream(out + f + qv * PER, pack16<T>(o + qv * PER));
-                } else {
-#pragma unroll
-                    for (int e = 0; e < EPT; ++e)
-                        if (mask & (1u << e)) out[f + e] = from_f32<T>(o[e]);
-                }
-            } else {
-                // General case (several boundaries, a row end, the stream end): a compact loop
-                // that reads its taps again from memory (L1-resident by now).
-                int64_t ce = c, te = t;
-                SeqCursor qe = q;
-#pragma unroll 1
-                for (int e = 0; e < EPT && f + e < total; ++e) {
-                    if (e > 0) {
-                        if (++te == Tn) {
-                            te = 0;
-                            ++ce;
-                            qe = locate(a, 0);
-                        }
-                        advance(a, qe, te);
-                    }
-                    if (qe.s >= 0 && qe.s < nseq && te - qe.bos >= K) {
-                        float w2[W], b2;
-                        load_filter1<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias,
-                                           a.bias_s, ce, w2, b2);
-                        const T* xr = x + ce * Tn;
-                        float acc = b2;
-#pragma unroll
-                        for (int k = 0; k < W; ++k) acc = fmaf(to_f32<T>(xr[te - K + k]), w2[k], acc);
-                        out[f + e] = from_f32<T>(activate<T>(acc, use_silu));
-                    }
-                }
-            }
-        }
-#pragma unroll
-        for (int qv = 0; qv < NV; ++qv) cur[qv] = nxt[qv];
-        // Advance this lane by one warp stride.
-        const int64_t c_prev = c;
-        if (Tn >= WSPAN) {
-            t += WSPAN;
-            if (t >= Tn) {
-                t -= Tn;
-                ++c;
-            }
-        } else {
-            const int64_t f2 = f + WSPAN;
-            c = f2 / Tn;
-            t = f2 - c * Tn;
-        }
-        if (c != c_prev) q = locate(a, t);
     }
 }
 
 // Second launch of the channel-first path: one thread per (channel, sequence) does the owner work
-// (initial state in, final state out, first W-1 outputs). The bulk pass above never writes those
-// outputs nor touches the cache, so the two launches do not overlap in what they write.
+// (initial state in, final state out, first W-1 outputs, which replace the bulk pass's values).
 template <typename T, int W>
 __global__ void __launch_bounds__(kBoundaryThreads) varlen_boundary_kernel(const VarArgs a) {
     const int64_t c = (int64_t)blockIdx.x * kBoundaryThreads + threadIdx.x;
@@ -582,7 +390,7 @@ constexpr int var_min_ctas() {
 }
 
 template <typename T, int W>
-cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
+cudaError_t run_varlen(const VarArgs& a, int dtype, cudaStream_t stream) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     const int64_t e = sizeof(T);
@@ -608,21 +416,27 @@ cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
         kern<<<dim3((unsigned)gx, (unsigned)gy), kVarThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
-    const bool cf = a.x_st == 1 && a.o_st == 1 && a.x_sd == a.T && a.o_sd == a.T && a.T >= kCfElems &&
-                    a.nseq <= 65535 && host_aligned16(a.x) && host_aligned16(a.out);
-    if (cf) {
-        const int64_t total = a.D * a.T;
-        const int64_t chunks = ceil_div(total, 32 * kCfElems);
-        // One wave of warps, each walking an equal run of chunks (as the channel-first prefill).
-        static int slot_cache[kSlotCacheDevices] = {};
-        const int64_t wave_warps =
-            std::max<int64_t>(1, device_slots((const void*)varlen_channel_first_kernel<T, W>,
-                                              kCfThreads, slot_cache)) * (kCfThreads / 32);
-        const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
-        const int64_t warps = ceil_div(chunks, iters);
-        varlen_channel_first_kernel<T, W>
-            <<<(unsigned)ceil_div(warps * 32, kCfThreads), kCfThreads, 0, stream>>>(a, total, iters);
-        cudaError_t err = cudaGetLastError();
+    if (a.x_st == 1 && a.o_st == 1 && a.x_sd == a.T && a.o_sd == a.T && a.nseq <= 65535) {
+        // Contiguous (D, T): the prefill of one (D, T) batch row, then the boundary pass.
+        FwdArgs f{};
+        f.x = a.x;
+        f.x_sb = a.D * a.T;
+        f.x_sd = a.T;
+        f.x_sl = 1;
+        f.w = a.w;
+        f.w_sd = a.w_sd;
+        f.w_sk = a.w_sk;
+        f.bias = a.bias;
+        f.bias_s = a.bias_s;
+        f.out = a.out;
+        f.o_sb = a.D * a.T;
+        f.o_sd = a.T;
+        f.o_sl = 1;
+        f.B = 1;
+        f.D = a.D;
+        f.L = a.T;
+        f.silu = a.silu;
+        cudaError_t err = launch_fwd(f, W, dtype, stream);
         if (err != cudaSuccess) return err;
         dim3 grid((unsigned)ceil_div(a.D, kBoundaryThreads), (unsigned)a.nseq);
         varlen_boundary_kernel<T, W><<<grid, kBoundaryThreads, 0, stream>>>(a);
@@ -639,7 +453,7 @@ cudaError_t run_varlen(const VarArgs& a, cudaStream_t stream) {
 
 cudaError_t launch_varlen(const VarArgs& a, int width, int dtype, cudaStream_t stream) {
     cudaError_t err = cudaErrorInvalidValue;
-    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_varlen<T, kW>(a, stream))));
+    CC1D_DISPATCH_DTYPE(dtype, CC1D_DISPATCH_WIDTH(width, err = (run_varlen<T, kW>(a, dtype, stream))));
     return err;
 }
 
