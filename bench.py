@@ -69,6 +69,8 @@ def parse():
     p.add_argument("--profile", choices=("fwd", "fwd_cf", "decode", "ring", "spec", "varlen", "varlen_cf"),
                    default=None,
                    help="run 4 launches of one kernel on a case larger than L2 (for ncu) and exit")
+    p.add_argument("--width", type=int, default=W,
+                   help="filter width of the --profile case (prefill and varlen cases)")
     return p.parse_args()
 
 
@@ -532,13 +534,13 @@ def sharded_check(rank, world, device):
     return bool(flag.item())
 
 
-def profile_case(case, device):
+def profile_case(case, device, width=W):
     """A few launches of one kernel, sized for an ncu capture (a few hundred MB on the device)."""
     import causal_conv1d_cute as C
 
     g = torch.Generator(device=device).manual_seed(0)
     bf = torch.bfloat16
-    w = (torch.rand(D, W, device=device, generator=g) - 0.5).to(bf)
+    w = (torch.rand(D, width, device=device, generator=g) - 0.5).to(bf)
     b = (torch.randn(D, device=device, generator=g) * 0.1).to(bf)
     if case == "fwd":  # config 2 with batch 2: 128 MiB in, 128 MiB out
         x = torch.randn(2, L, D, device=device, generator=g).to(bf)
@@ -572,7 +574,7 @@ def profile_case(case, device):
         xv = torch.randn(T, D, device=device, generator=g).to(bf)
         if case == "varlen_cf":  # channel-first: contiguous (8192, T); the call gets x = xv.t()
             xv = xv.t().contiguous().t()
-        states = torch.randn(64, D, 3, device=device, generator=g).to(bf)
+        states = torch.randn(64, D, width - 1, device=device, generator=g).to(bf)
         cidx = torch.arange(8, device=device, dtype=torch.int32) * 3
         hinit = torch.ones(8, dtype=torch.bool, device=device)
         calls = [lambda: C.causal_conv1d_varlen_fn(xv.t(), w, None, qsl, cidx, hinit, states, "silu")] * 4
@@ -588,7 +590,7 @@ def profile_case(case, device):
 def main():
     args = parse()
     if args.profile:
-        profile_case(args.profile, torch.device("cuda", 0))
+        profile_case(args.profile, torch.device("cuda", 0), args.width)
         return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
