@@ -122,6 +122,14 @@ template <typename T>
 __device__ __forceinline__ void set_lane(uint4& v, int i, T val) {
     reinterpret_cast<T*>(&v)[i] = val;
 }
+template <typename T>
+__device__ __forceinline__ T lane_of(const uint2& v, int i) {
+    return reinterpret_cast<const T*>(&v)[i];
+}
+template <typename T>
+__device__ __forceinline__ void set_lane(uint2& v, int i, T val) {
+    reinterpret_cast<T*>(&v)[i] = val;
+}
 
 // ---------------------------------------------------------------------------------------------
 // Global memory access
@@ -171,6 +179,83 @@ __device__ __forceinline__ void st16_stream(void* p, const uint4& v) {
     asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
                  "r"(v.z), "r"(v.w)
                  : "memory");
+}
+
+// A thread's channel vector of NB bytes (16: uint4, 8: uint2) for the kernels that can run with
+// half-width vectors (fewer registers per thread when the filter is wide).
+template <int NB>
+struct RawVec;
+template <>
+struct RawVec<16> {
+    using type = uint4;
+};
+template <>
+struct RawVec<8> {
+    using type = uint2;
+};
+
+template <int NB>
+__device__ __forceinline__ typename RawVec<NB>::type ldg_stream_raw(const void* p) {
+    if constexpr (NB == 16) {
+        return ldg16_stream(p);
+    } else {
+        uint2 v;
+        asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];"
+                     : "=r"(v.x), "=r"(v.y)
+                     : "l"(p));
+        return v;
+    }
+}
+
+template <int NB>
+__device__ __forceinline__ void st_stream_raw(void* p, const typename RawVec<NB>::type& v) {
+    if constexpr (NB == 16) {
+        st16_stream(p, v);
+    } else {
+        asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(v.x), "r"(v.y)
+                     : "memory");
+    }
+}
+
+template <int NB>
+__device__ __forceinline__ typename RawVec<NB>::type ldg_raw(const void* p) {
+    return __ldg(reinterpret_cast<const typename RawVec<NB>::type*>(p));
+}
+
+// Coherent NB-byte load and store (conv state caches, which the same kernel writes).
+template <int NB>
+__device__ __forceinline__ typename RawVec<NB>::type ld_raw(const void* p) {
+    return *reinterpret_cast<const typename RawVec<NB>::type*>(p);
+}
+template <int NB>
+__device__ __forceinline__ void st_raw(void* p, const typename RawVec<NB>::type& v) {
+    *reinterpret_cast<typename RawVec<NB>::type*>(p) = v;
+}
+
+// NB-byte vector <-> NB / sizeof(T) fp32 lanes.
+template <typename T, int NB>
+__device__ __forceinline__ void unpack_raw(const typename RawVec<NB>::type& v, float* f) {
+    if constexpr (NB == 16) {
+        unpack16<T>(v, f);
+    } else {
+        float g[Vec<T>::V];
+        unpack16<T>(make_uint4(v.x, v.y, 0u, 0u), g);
+#pragma unroll
+        for (int i = 0; i < NB / (int)sizeof(T); ++i) f[i] = g[i];
+    }
+}
+
+template <typename T, int NB>
+__device__ __forceinline__ typename RawVec<NB>::type pack_raw(const float* f) {
+    if constexpr (NB == 16) {
+        return pack16<T>(f);
+    } else {
+        float g[Vec<T>::V];
+#pragma unroll
+        for (int i = 0; i < Vec<T>::V; ++i) g[i] = i < NB / (int)sizeof(T) ? f[i] : 0.f;
+        const uint4 u = pack16<T>(g);
+        return make_uint2(u.x, u.y);
+    }
 }
 
 __device__ __forceinline__ bool aligned16(const void* p) {
@@ -263,18 +348,20 @@ __device__ __forceinline__ void flag_status(int32_t* status, int32_t bits) {
 // own (dim, W) tensor read in place: when it is contiguous and 16-byte aligned (wvec) the V*W
 // elements of a channel group are W whole 16-byte vectors, otherwise they are read one by one.
 // bvec: the bias is contiguous and 16-byte aligned.
-template <typename T, int W>
+// NB: bytes of channels per thread (16, or 8 for the half-width kernels); V = NB / sizeof(T).
+template <typename T, int W, int NB = 16>
 __device__ __forceinline__ void load_filter(const T* __restrict__ weight, int64_t w_sd,
                                             int64_t w_sk, const T* __restrict__ bias,
                                             int64_t bias_s, int64_t c0, bool wvec, bool bvec,
-                                            float (&w)[W][Vec<T>::V], float (&b)[Vec<T>::V]) {
-    constexpr int V = Vec<T>::V;
+                                            float (&w)[W][NB / sizeof(T)],
+                                            float (&b)[NB / sizeof(T)]) {
+    constexpr int V = NB / (int)sizeof(T);
     if (wvec) {
         const T* base = weight + c0 * W;
 #pragma unroll
         for (int q = 0; q < W; ++q) {
             float f[V];
-            unpack16<T>(ldg16(base + q * V), f);
+            unpack_raw<T, NB>(ldg_raw<NB>(base + q * V), f);
 #pragma unroll
             for (int i = 0; i < V; ++i) {
                 const int flat = q * V + i;  // = e * W + k
@@ -292,7 +379,7 @@ __device__ __forceinline__ void load_filter(const T* __restrict__ weight, int64_
 #pragma unroll
         for (int e = 0; e < V; ++e) b[e] = 0.f;
     } else if (bvec) {
-        unpack16<T>(ldg16(bias + c0), b);
+        unpack_raw<T, NB>(ldg_raw<NB>(bias + c0), b);
     } else {
 #pragma unroll
         for (int e = 0; e < V; ++e) b[e] = to_f32<T>(__ldg(bias + (c0 + e) * bias_s));

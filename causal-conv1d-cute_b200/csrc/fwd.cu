@@ -58,10 +58,10 @@ __global__ void __launch_bounds__(NT)
 // W-1 rows before each batch stretch. Every CTA does the same work whatever B and L are (no
 // partial last wave), and the CTAs of one share, launched back to back, read the same token rows
 // at about the same time, so each DRAM page is opened once for all its channel blocks.
-template <typename T, int W, int U, bool PF, int NT, int MINB>
+template <typename T, int W, int U, bool PF, int NT, int MINB, int NB = 16>
 __global__ void __launch_bounds__(NT, MINB)
     fwd_channel_last_share_kernel(const FwdArgs a, bool wvec, bool bvec) {
-    constexpr int V = Vec<T>::V;
+    constexpr int V = NB / (int)sizeof(T);
     const int64_t nvec = a.D / V;
     const int64_t j = (int64_t)blockIdx.x * NT + threadIdx.x;
     if (j >= nvec) return;
@@ -71,9 +71,9 @@ __global__ void __launch_bounds__(NT, MINB)
     const bool use_silu = a.silu != 0;
     const int64_t c0 = j * V;
     float w[W][V], bv[V];
-    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
-                      w, bv);
-    prescale_filter<T, W>(w, bv, use_silu);
+    load_filter<T, W, NB>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
+                          bvec, w, bv);
+    prescale_filter<T, W, NB>(w, bv, use_silu);
     while (r < end) {
         const int64_t b = r / a.L;
         const int64_t t0 = r - b * a.L;
@@ -81,8 +81,8 @@ __global__ void __launch_bounds__(NT, MINB)
         const T* xb = (const T*)a.x + b * a.x_sb + c0;
         T* ob = (T*)a.out + b * a.o_sb + c0;
         float h[W - 1][V];
-        load_halo<T, W>(xb, a.x_sl, t0, h);
-        walk_strip<T, W, U, PF>(xb, a.x_sl, ob, a.o_sl, t0, t0 + n, h, w, bv, use_silu);
+        load_halo<T, W, NB>(xb, a.x_sl, t0, h);
+        walk_strip<T, W, U, PF, NB>(xb, a.x_sl, ob, a.o_sl, t0, t0 + n, h, w, bv, use_silu);
         r += n;
     }
 }
@@ -294,17 +294,32 @@ __global__ void __launch_bounds__(kGenThreads)
 constexpr int64_t kStripRows = 128;
 constexpr int64_t kMinShareRows = 16;
 
-// Rows in flight per thread (U) and minimum resident CTAs per SM in the launch bounds of the
-// balanced walk (0: the compiler's own register budget). Measured on B200 at the config-2 shape,
-// one launch at a time (W: us for U = 8 with the compiler's budget / U = 8 with minimum 1 /
-// U = 6 with minimum 1): 4: 182.6 / 196.2 / 183.1; 5: 200.5 / 197.4 / 184.4;
-// 6: 204.6 / 201.6 / 218.7; 7: 206.1 / 202.1 / 219.3; 8: 217.9 / 207.7 / 227.0.
-template <int W>
-constexpr int share_rows() {
-    return W == 5 ? 6 : 8;
+// Launch table of the balanced walk: bytes of channels per thread (NB), rows in flight per thread
+// (U), CTA size and minimum resident CTAs per SM in the launch bounds (0: the compiler's own
+// register budget). With 16-byte vectors (8 bf16 channels per thread) the filter and window of a
+// wide filter take most of the registers: at W = 8 the walk needed 234 registers, so only 8 warps
+// per SM held loads in flight. From W = 5, 16-bit types use 8-byte vectors (4 channels per
+// thread) with 16 rows in flight. Measured on B200 at the config-2 shape, one launch at a time
+// (16-byte / 8-byte vectors, us): W = 4: 182.0 / 183.9; 5: 188.0 / 184.4 (128-thread CTAs);
+// 6: 204.9 / 185.7 (minimum 6 CTAs); 8: 210.2 / 196.2. Earlier 16-byte measurements (W: U = 8
+// with the compiler's budget / U = 8 with minimum 1 / U = 6 with minimum 1): 4: 182.6 / 196.2 /
+// 183.1; 5: 200.5 / 197.4 / 184.4; 6: 204.6 / 201.6 / 218.7; 7: 206.1 / 202.1 / 219.3;
+// 8: 217.9 / 207.7 / 227.0. fp32 keeps 16-byte vectors, which hold 4 channels already.
+template <typename T, int W>
+constexpr int share_bytes() {
+    return sizeof(T) == 2 && W >= 5 ? 8 : 16;
 }
-template <int W>
+template <typename T, int W>
+constexpr int share_rows() {
+    return share_bytes<T, W>() == 8 ? 16 : (W == 5 ? 6 : 8);
+}
+template <typename T, int W>
+constexpr int share_threads() {
+    return share_bytes<T, W>() == 8 && W == 5 ? 128 : 64;
+}
+template <typename T, int W>
 constexpr int share_min_ctas() {
+    if (share_bytes<T, W>() == 8) return W == 6 ? 6 : 1;
     return W >= 5 ? 1 : 0;
 }
 
@@ -320,10 +335,13 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     if (cl) {
         const int64_t nvec = a.D / V;
         const int64_t gx = ceil_div(nvec, (int64_t)kClThreads);
+        constexpr int SB = share_bytes<T, W>();
+        constexpr int SNT = share_threads<T, W>();
+        const int64_t sgx = ceil_div(a.D / (SB / (int64_t)sizeof(T)), (int64_t)SNT);
         static int slot_cache[kSlotCacheDevices] = {};
-        auto share = fwd_channel_last_share_kernel<T, W, share_rows<W>(), true, kClThreads,
-                                                   share_min_ctas<W>()>;
-        const int64_t slots = device_slots((const void*)share, kClThreads, slot_cache);
+        auto share = fwd_channel_last_share_kernel<T, W, share_rows<T, W>(), true, SNT,
+                                                   share_min_ctas<T, W>(), SB>;
+        const int64_t slots = device_slots((const void*)share, SNT, slot_cache);
         const int64_t strip = std::max<int64_t>(1, std::min<int64_t>(a.L, kStripRows));
         const int64_t nstrips = ceil_div(a.L, strip);
         if ((W <= 3 || a.L <= kStripRows) && a.B * nstrips * gx * 2 >= slots) {
@@ -333,9 +351,9 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
             return cudaGetLastError();
         }
         const int64_t gy = std::max<int64_t>(
-            1, std::min<int64_t>({std::max<int64_t>(slots, 1) / gx,
+            1, std::min<int64_t>({std::max<int64_t>(slots, 1) / sgx,
                                   ceil_div(a.B * a.L, kMinShareRows), 65535}));
-        share<<<dim3((unsigned)gx, (unsigned)gy), kClThreads, 0, stream>>>(a, wvec, bvec);
+        share<<<dim3((unsigned)sgx, (unsigned)gy), SNT, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     const bool rows_dense = a.x_sl == 1 && a.o_sl == 1 && a.x_sd == a.L && a.o_sd == a.L &&

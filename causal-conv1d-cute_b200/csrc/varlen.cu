@@ -83,20 +83,21 @@ __device__ __forceinline__ SeqSlot seq_slot(const VarArgs& a, int64_t s, bool re
 // write the final state (the last W-1 inputs of [initial state | sequence], as raw bits) and leave
 // the initial state in the fp32 window h. The final state is written before the walk, so the
 // raw initial state does not stay live across it.
-template <typename T, int W>
+template <typename T, int W, int NB>
 __device__ __forceinline__ void owner_state(const VarArgs& a, const T* xb, int64_t c0, int64_t s,
                                             int64_t bos, int64_t eos, bool report,
-                                            float (&h)[W - 1][Vec<T>::V]) {
-    constexpr int V = Vec<T>::V;
+                                            float (&h)[W - 1][NB / sizeof(T)]) {
+    constexpr int V = NB / (int)sizeof(T);
     constexpr int K = W - 1;
+    using R = typename RawVec<NB>::type;
     if (report) check_bounds(a, s);
     const SeqSlot ss = seq_slot(a, s, report);
     T* sp = ss.live ? (T*)a.states + ss.slot * a.s_slot + c0 * K : nullptr;
-    uint4 init[K];
+    R init[K];
     if (ss.use_init) {
-        uint4 blk[K];
+        R blk[K];
 #pragma unroll
-        for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
+        for (int q = 0; q < K; ++q) blk[q] = ld_raw<NB>(sp + q * V);
 #pragma unroll
         for (int ee = 0; ee < V; ++ee)
 #pragma unroll
@@ -106,28 +107,28 @@ __device__ __forceinline__ void owner_state(const VarArgs& a, const T* xb, int64
             }
     } else {
 #pragma unroll
-        for (int k = 0; k < K; ++k) init[k] = make_uint4(0, 0, 0, 0);
+        for (int k = 0; k < K; ++k) init[k] = R{};
     }
 #pragma unroll
-    for (int k = 0; k < K; ++k) unpack16<T>(init[k], h[k]);
+    for (int k = 0; k < K; ++k) unpack_raw<T, NB>(init[k], h[k]);
     if (!ss.live) return;
     const int64_t n = eos - bos;
-    uint4 fin[K];
+    R fin[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) {
         const int64_t pos = eos - K + k;
         if (pos >= bos) {
-            fin[k] = ldg16(xb + pos * a.x_st);
+            fin[k] = ldg_raw<NB>(xb + pos * a.x_st);
         } else {
             // n < K: entry k + n of the initial state.
             const int64_t m = k + n;
-            uint4 v = init[0];
+            R v = init[0];
 #pragma unroll
             for (int q = 1; q < K; ++q) v = (m == q) ? init[q] : v;
             fin[k] = v;
         }
     }
-    uint4 blk[K];
+    R blk[K];
 #pragma unroll
     for (int q = 0; q < K; ++q)
 #pragma unroll
@@ -136,23 +137,24 @@ __device__ __forceinline__ void owner_state(const VarArgs& a, const T* xb, int64
             set_lane<T>(blk[q], i, lane_of<T>(fin[flat % K], flat / K));
         }
 #pragma unroll
-    for (int q = 0; q < K; ++q) st16(sp + q * V, blk[q]);
+    for (int q = 0; q < K; ++q) st_raw<NB>(sp + q * V, blk[q]);
 }
 
-template <typename T, int W, int U, bool PF, int NT, int MINB>
+// NB: bytes of channels per thread (16, or 8 for wide filters; see the launch table).
+template <typename T, int W, int U, bool PF, int NT, int MINB, int NB>
 __global__ void __launch_bounds__(NT, MINB)
     varlen_token_major_kernel(const VarArgs a, bool wvec, bool bvec) {
-    constexpr int V = Vec<T>::V;
+    constexpr int V = NB / (int)sizeof(T);
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
     const int64_t j = (int64_t)blockIdx.x * NT + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
     float w[W][V], bv[V];
-    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
-                      w, bv);
+    load_filter<T, W, NB>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
+                          bvec, w, bv);
     const bool use_silu = a.silu != 0;
-    prescale_filter<T, W>(w, bv, use_silu);
+    prescale_filter<T, W, NB>(w, bv, use_silu);
     const T* xb = (const T*)a.x + c0;
     T* ob = (T*)a.out + c0;
     // This CTA's share of the packed tokens: [t0, t1), one of gridDim.y equal parts.
@@ -178,16 +180,17 @@ __global__ void __launch_bounds__(NT, MINB)
             if (t == bos) {
                 // Owner of sequence s: initial state in, final state out, then the walk starts
                 // at the sequence start and runs past the strip end over the first W-1 tokens.
-                owner_state<T, W>(a, xb, c0, s, bos, eos, j == 0, h);
+                owner_state<T, W, NB>(a, xb, c0, s, bos, eos, j == 0, h);
                 ta = bos;
                 tb = min(eos, max(e, bos + K));
             } else {
                 // Tokens less than W-1 after the sequence start belong to its owner.
                 ta = max(t, bos + K);
                 tb = e;
-                if (ta < tb) load_halo<T, W>(xb, a.x_st, ta, h);  // rows >= bos
+                if (ta < tb) load_halo<T, W, NB>(xb, a.x_st, ta, h);  // rows >= bos
             }
-            if (ta < tb) walk_strip<T, W, U, PF>(xb, a.x_st, ob, a.o_st, ta, tb, h, w, bv, use_silu);
+            if (ta < tb)
+                walk_strip<T, W, U, PF, NB>(xb, a.x_st, ob, a.o_st, ta, tb, h, w, bv, use_silu);
             t = e;
             if (e == eos) ++s;
         }
@@ -376,17 +379,29 @@ __global__ void __launch_bounds__(kGenThreads) varlen_generic_kernel(const VarAr
 constexpr int64_t kStripTokens = 128;
 constexpr int64_t kMinShareTokens = 16;
 
-// Rows in flight per thread (U) and minimum resident CTAs per SM in the launch bounds of the
-// token-major walk. Measured on B200 with the config-5 batch, one balanced wave (W: us with
-// U = 8 / U = 6, minimum 1 CTA; U = 6 with minimum 6 CTAs): 4: 230.4 / 231.2; 5: 244.6 / 231.1;
-// 6: 248.3 / 268.0, 236.2 with minimum 6; 8: 256.1 / 278.3.
-template <int W>
-constexpr int var_rows() {
-    return W == 5 || W == 6 ? 6 : 8;
+// Launch table of the token-major walk: bytes of channels per thread (NB), rows in flight per
+// thread (U), CTA size and minimum resident CTAs per SM in the launch bounds (0: the compiler's own
+// register budget). As in the channel-last prefill, 16-bit types switch to 8-byte vectors
+// (4 channels per thread, 16 rows in flight) from W = 5, where the filter and window of 8 channels
+// left too few warps per SM. Earlier 16-byte measurements on B200 with the config-5 batch, one
+// balanced wave (W: us with U = 8 / U = 6, minimum 1 CTA; U = 6 with minimum 6 CTAs):
+// 4: 230.4 / 231.2; 5: 244.6 / 231.1; 6: 248.3 / 268.0, 236.2 with minimum 6; 8: 256.1 / 278.3.
+template <typename T, int W>
+constexpr int var_bytes() {
+    return sizeof(T) == 2 && W >= 5 ? 8 : 16;
 }
-template <int W>
+template <typename T, int W>
+constexpr int var_rows() {
+    return var_bytes<T, W>() == 8 ? 16 : (W == 5 || W == 6 ? 6 : 8);
+}
+template <typename T, int W>
+constexpr int var_threads() {
+    return var_bytes<T, W>() == 8 && W == 5 ? 128 : kVarThreads;
+}
+template <typename T, int W>
 constexpr int var_min_ctas() {
-    return W == 6 ? 6 : 0;  // 0: no minimum, the compiler's own register budget
+    if (var_bytes<T, W>() == 8) return W == 6 ? 6 : 1;
+    return W == 6 ? 6 : 0;
 }
 
 template <typename T, int W>
@@ -402,18 +417,20 @@ cudaError_t run_varlen(const VarArgs& a, int dtype, cudaStream_t stream) {
     const bool tm = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
                     host_aligned16(a.out) && (a.x_st * e) % 16 == 0 && (a.o_st * e) % 16 == 0;
     if (tm && sok) {
-        const int64_t gx = ceil_div(a.D / V, (int64_t)kVarThreads);
+        constexpr int NB = var_bytes<T, W>();
+        constexpr int NT = var_threads<T, W>();
+        const int64_t gx = ceil_div(a.D / (NB / e), (int64_t)NT);
         static int slot_cache[kSlotCacheDevices] = {};
-        auto kern =
-            varlen_token_major_kernel<T, W, var_rows<W>(), true, kVarThreads, var_min_ctas<W>()>;
-        const int64_t slots = device_slots((const void*)kern, kVarThreads, slot_cache);
+        auto kern = varlen_token_major_kernel<T, W, var_rows<T, W>(), true, NT,
+                                              var_min_ctas<T, W>(), NB>;
+        const int64_t slots = device_slots((const void*)kern, NT, slot_cache);
         const int64_t strips = ceil_div(a.T, kStripTokens);
         const int64_t shares = W == 2 && strips * gx * 2 >= slots
                                    ? strips
                                    : std::min<int64_t>(std::max<int64_t>(slots, 1) / gx,
                                                        ceil_div(a.T, kMinShareTokens));
         const int64_t gy = std::max<int64_t>(1, std::min<int64_t>(shares, 65535));
-        kern<<<dim3((unsigned)gx, (unsigned)gy), kVarThreads, 0, stream>>>(a, wvec, bvec);
+        kern<<<dim3((unsigned)gx, (unsigned)gy), NT, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     if (a.x_st == 1 && a.o_st == 1 && a.x_sd == a.T && a.o_sd == a.T && a.nseq <= 65535) {

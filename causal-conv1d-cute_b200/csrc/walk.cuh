@@ -20,12 +20,12 @@ __host__ __device__ constexpr bool prescaled_silu() {
     return !std::is_same<T, float>::value;
 }
 
-template <typename T, int W>
-__device__ __forceinline__ void prescale_filter(float (&w)[W][Vec<T>::V], float (&b)[Vec<T>::V],
-                                                bool use_silu) {
+template <typename T, int W, int NB = 16>
+__device__ __forceinline__ void prescale_filter(float (&w)[W][NB / sizeof(T)],
+                                                float (&b)[NB / sizeof(T)], bool use_silu) {
     if (prescaled_silu<T>() && use_silu) {
 #pragma unroll
-        for (int e = 0; e < Vec<T>::V; ++e) {
+        for (int e = 0; e < NB / (int)sizeof(T); ++e) {
 #pragma unroll
             for (int k = 0; k < W; ++k) w[k][e] *= 0.5f;
             b[e] *= 0.5f;
@@ -43,12 +43,12 @@ __device__ __forceinline__ float activate_prescaled(float acc, bool use_silu) {
 // One output vector from the fp32 window h (oldest first) and the new input xv; shifts xv into
 // the window afterwards. Bias first, taps oldest first, one fused multiply-add per tap. The
 // filter is prescaled (prescale_filter).
-template <typename T, int W>
-__device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const float* xv,
-                                          const float (&w)[W][Vec<T>::V],
-                                          const float (&bv)[Vec<T>::V], bool use_silu,
+template <typename T, int W, int NB = 16>
+__device__ __forceinline__ void conv_step(float (&h)[W - 1][NB / sizeof(T)], const float* xv,
+                                          const float (&w)[W][NB / sizeof(T)],
+                                          const float (&bv)[NB / sizeof(T)], bool use_silu,
                                           float* o) {
-    constexpr int V = Vec<T>::V;
+    constexpr int V = NB / (int)sizeof(T);
     constexpr int K = W - 1;
 #pragma unroll
     for (int e = 0; e < V; ++e) {
@@ -69,37 +69,38 @@ __device__ __forceinline__ void conv_step(float (&h)[W - 1][Vec<T>::V], const fl
 // Walk rows [ta, tb) of one channel group: h holds the W-1 previous inputs (fp32, oldest first).
 // Rows are loaded U at a time; with PF the next U rows are requested before the current U are
 // computed, so 2U 16-byte loads per thread stay in flight (bytes in flight per SM bound this
-// kernel).
-template <typename T, int W, int U, bool PF>
+// kernel). NB: bytes of channels per thread (16, or 8 for the half-width kernels).
+template <typename T, int W, int U, bool PF, int NB = 16>
 __device__ __forceinline__ void walk_strip(const T* __restrict__ xb, int64_t x_st,
                                            T* __restrict__ ob, int64_t o_st, int64_t ta,
-                                           int64_t tb, float (&h)[W - 1][Vec<T>::V],
-                                           const float (&w)[W][Vec<T>::V],
-                                           const float (&bv)[Vec<T>::V], bool use_silu) {
-    constexpr int V = Vec<T>::V;
+                                           int64_t tb, float (&h)[W - 1][NB / sizeof(T)],
+                                           const float (&w)[W][NB / sizeof(T)],
+                                           const float (&bv)[NB / sizeof(T)], bool use_silu) {
+    constexpr int V = NB / (int)sizeof(T);
+    using R = typename RawVec<NB>::type;
     int64_t t = ta;
-    auto emit = [&](const uint4& r, int64_t row) {
+    auto emit = [&](const R& r, int64_t row) {
         float xv[V], o[V];
-        unpack16<T>(r, xv);
-        conv_step<T, W>(h, xv, w, bv, use_silu, o);
-        st16_stream(ob + row * o_st, pack16<T>(o));
+        unpack_raw<T, NB>(r, xv);
+        conv_step<T, W, NB>(h, xv, w, bv, use_silu, o);
+        st_stream_raw<NB>(ob + row * o_st, pack_raw<T, NB>(o));
     };
     if (PF) {
-        uint4 nxt[U];
+        R nxt[U];
         bool have = t + U <= tb;
         if (have) {
 #pragma unroll
-            for (int i = 0; i < U; ++i) nxt[i] = ldg16_stream(xb + (t + i) * x_st);
+            for (int i = 0; i < U; ++i) nxt[i] = ldg_stream_raw<NB>(xb + (t + i) * x_st);
         }
         while (have) {
-            uint4 cur[U];
+            R cur[U];
 #pragma unroll
             for (int i = 0; i < U; ++i) cur[i] = nxt[i];
             const int64_t tn = t + U;
             have = tn + U <= tb;
             if (have) {
 #pragma unroll
-                for (int i = 0; i < U; ++i) nxt[i] = ldg16_stream(xb + (tn + i) * x_st);
+                for (int i = 0; i < U; ++i) nxt[i] = ldg_stream_raw<NB>(xb + (tn + i) * x_st);
             }
 #pragma unroll
             for (int i = 0; i < U; ++i) emit(cur[i], t + i);
@@ -107,14 +108,14 @@ __device__ __forceinline__ void walk_strip(const T* __restrict__ xb, int64_t x_s
         }
     } else {
         for (; t + U <= tb; t += U) {
-            uint4 r[U];
+            R r[U];
 #pragma unroll
-            for (int i = 0; i < U; ++i) r[i] = ldg16_stream(xb + (t + i) * x_st);
+            for (int i = 0; i < U; ++i) r[i] = ldg_stream_raw<NB>(xb + (t + i) * x_st);
 #pragma unroll
             for (int i = 0; i < U; ++i) emit(r[i], t + i);
         }
     }
-    for (; t < tb; ++t) emit(ldg16_stream(xb + t * x_st), t);
+    for (; t < tb; ++t) emit(ldg_stream_raw<NB>(xb + t * x_st), t);
 }
 
 // conv_step with per-token sequence ids: a history tap counts only when its id equals the
@@ -199,17 +200,17 @@ __device__ __forceinline__ void walk_strip_seq(const T* __restrict__ xb, int64_t
 }
 
 // Window of the W-1 rows before t0 (zeros before the sequence start).
-template <typename T, int W>
+template <typename T, int W, int NB = 16>
 __device__ __forceinline__ void load_halo(const T* xb, int64_t x_st, int64_t t0,
-                                          float (&h)[W - 1][Vec<T>::V]) {
+                                          float (&h)[W - 1][NB / sizeof(T)]) {
 #pragma unroll
     for (int k = 0; k < W - 1; ++k) {
         const int64_t t = t0 - (W - 1) + k;
         if (t >= 0) {
-            unpack16<T>(ldg16(xb + t * x_st), h[k]);
+            unpack_raw<T, NB>(ldg_raw<NB>(xb + t * x_st), h[k]);
         } else {
 #pragma unroll
-            for (int e = 0; e < Vec<T>::V; ++e) h[k][e] = 0.f;
+            for (int e = 0; e < NB / (int)sizeof(T); ++e) h[k][e] = 0.f;
         }
     }
 }
