@@ -6,6 +6,8 @@ lengths and the GPU's resident-CTA count. These cases sit on both sides of that 
 that cross batch and sequence boundaries and a partial last channel block, and check that the
 result is bit-identical to the scalar path (the same arithmetic in the same order, reached by
 viewing rows of a wider buffer that are not 16-byte aligned), and, for a small case, to the oracle.
+From W = 5 the 16-bit walks give each thread 4 channels (8-byte vectors); the W = 5..8 cases, with
+channel counts that leave a partial last CTA of 64 or 128 threads, cover that form.
 """
 
 import numpy as np
@@ -19,7 +21,8 @@ from causal_conv1d_cute import causal_conv1d_fn, causal_conv1d_varlen_fn
 PAD = -1
 
 # (B, L, D, W): W = 2 strips over many CTAs; short sequences (one strip each, enough CTAs);
-# balanced shares crossing batch boundaries; shares with a partial channel block; long shares.
+# balanced shares crossing batch boundaries; shares with a partial channel block; long shares;
+# half-width walks (W >= 5) with partial 128- and 64-thread channel blocks.
 FWD_SHAPES = [
     (8, 1000, 8192, 2),
     (64, 100, 4096, 4),
@@ -27,6 +30,8 @@ FWD_SHAPES = [
     (3, 1000, 2304, 8),
     (2, 5000, 1024, 3),
     (1, 17, 64, 6),
+    (2, 700, 1000, 5),
+    (3, 333, 776, 7),
 ]
 
 
@@ -67,6 +72,8 @@ VARLEN_CASES = [
     (_lengths(2, 32, 7.0), 512, 3),
     (_lengths(3, 32, 7.0), 768, 8),
     ([1, 2, 3, 0, 9, 1, 700, 2, 5], 1024, 8),
+    (_lengths(4, 20, 6.0), 1000, 5),
+    (_lengths(5, 12, 6.5), 776, 6),
 ]
 
 
