@@ -21,11 +21,11 @@ all-gather a sample of every rank's outputs and compare them bit for bit with th
 
 With N = 1 the other BASELINE paths are measured too ("paths"): config 2 stored channel-first,
 config 2 with initial and final states and with sequence ids (the Dao-interface extras), indexed
-decode (config 3) and its ring variant with the to_ring / from_ring conversions, the 4-step
-speculative verify with dense per-step states
-(config 4), and packed varlen prefill (config 5) at widths 2, 3, 4 and 8, token-major and
-channel-first, each replayed in a CUDA
-graph (no host launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
+decode (config 3) and its ring variant with the to_ring / from_ring conversions, direct-state
+decode at B = 256 and 64 and ring decode at B = 64 (the shapes of the reference's published
+decode numbers), the 4-step speculative verify with dense per-step states (config 4), and packed
+varlen prefill (config 5) at widths 2, 3, 4 and 8, token-major and channel-first, each replayed in
+a CUDA graph (no host launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
 exceeds L2, and "warm" repeats one set.
 
 --impl reference times the reference's CPU algorithm (the C port of its PyTorch fallback,
@@ -396,6 +396,24 @@ def run_paths(device, reps=50, sets=8):
         calls.append(lambda x=x, cache=cache, idx=idx: C.causal_conv1d_update(x, cache, w4, bias, "silu", idx))
     nbytes = 2 * Bd * D * 2 + 2 * Bd * D * 3 * 2 + D * 4 * 2 + D * 2 + Bd * 4
     record("decode_indexed_b256", calls, nbytes)
+
+    # The reference's published decode shapes (B300): direct (non-indexed) state at B = 256 and
+    # B = 64, and ring decode at B = 64, for a like-for-like comparison.
+    for Bq in (256, 64):
+        calls = []
+        for _ in range(sets):
+            x = torch.randn(Bq, D, device=device, generator=g).to(bf)
+            st = torch.randn(Bq, D, 3, device=device, generator=g).to(bf)
+            calls.append(lambda x=x, st=st: C.causal_conv1d_update(x, st, w4, bias, "silu"))
+        nbytes = 2 * Bq * D * 2 + 2 * Bq * D * 3 * 2 + D * 4 * 2 + D * 2
+        record(f"decode_direct_b{Bq}", calls, nbytes)
+    calls = []
+    for _ in range(sets):
+        x = torch.randn(64, D, device=device, generator=g).to(bf)
+        ring = torch.randn(64, 3, D, device=device, generator=g).to(bf)
+        seen = torch.randint(1, 8193, (64,), device=device, generator=g, dtype=torch.int32)
+        calls.append(lambda x=x, ring=ring, seen=seen: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen))
+    record("decode_ring_b64", calls, 2 * 64 * D * 2 + 4 * 64 * D * 2 + D * 4 * 2 + D * 2 + 64 * 4)
 
     # Config 3 ring variant: ring (256, 3, 8192), seen ~U[1, 8192].
     calls = []
