@@ -11,8 +11,9 @@ causal_conv1d_fn call over that batch. value = algorithmic bytes (every input el
 every output element written once, plus weights and bias) / device time, summed over ranks.
 Inputs (512 MiB) exceed L2 (126 MB), so no flush is needed between steps. e2e is the same
 metric with the input in pinned host memory and the result read back to it inside every step:
-the public causal_conv1d_fn is called once per batch row, and rows are pipelined over three
-streams (upload of row b + 1, convolution of row b, download of row b - 1).
+the public causal_conv1d_fn is called once per 1024-token chunk of each batch row (over a window
+that starts W - 1 tokens earlier, so each output has its full history), and chunks are pipelined
+over three streams (upload of chunk i + 1, convolution of chunk i, download of chunk i - 1).
 
 At N > 1 (torchrun, one rank per GPU) the layer is channel-sliced as tensor parallelism shards it:
 rank r owns channels [8192 r, 8192 (r + 1)) of a layer with 8192 N channels, so per-GPU work is
@@ -57,6 +58,7 @@ HEADLINE_BYTES = 2 * B * L * D * E + D * W * E + D * E  # 1,073,823,744
 # The kernel the headline call dispatches to (balanced shares: W = 4, 4096-token sequences).
 HEADLINE_KERNEL = "fwd_channel_last_share_kernel"
 L2_BYTES = 126 * 2**20
+E2E_CHUNKS = 4  # token chunks per batch row in the e2e pipeline
 
 
 def parse():
@@ -234,14 +236,19 @@ def run_headline(args, rank, world, device):
     avg_launch_ms = statistics.mean(per)
 
     # End to end through the public API: pinned host input in, result back to pinned host memory.
-    # The batch rows are pipelined over three streams: row b + 1 uploads while row b is convolved
-    # and row b - 1 downloads (PCIe carries both directions at once). Every step moves the whole
-    # input in and the whole result out; the step ends when the last row is back on the host.
+    # Every batch row is cut into E2E_CHUNKS token chunks, pipelined over three streams: chunk
+    # i + 1 uploads while chunk i is convolved and chunk i - 1 downloads (PCIe carries both
+    # directions at once; more, smaller chunks shorten the pipeline's fill and drain). Chunk k > 0
+    # of a row is convolved over the window that starts W - 1 tokens earlier (already on the
+    # device), into its own output buffer whose first W - 1 rows are discarded, so every output is
+    # computed from its full history. Every step moves the whole input in and the whole result
+    # out; the step ends when the last chunk is back on the host.
+    Lc = L // E2E_CHUNKS
     xh = torch.empty(B, L, D, dtype=torch.bfloat16, pin_memory=True)
     xh.copy_(x)
     oh = torch.empty(B, L, D, dtype=torch.bfloat16, pin_memory=True)
     xd = torch.empty_like(x)
-    yd = torch.empty_like(x)
+    yc = torch.empty(B, E2E_CHUNKS, Lc + W - 1, D, device=device, dtype=torch.bfloat16)
     s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
 
     def e2e_step():
@@ -251,19 +258,23 @@ def run_headline(args, rank, world, device):
         for s_ in (s_in, s_cmp, s_out):
             s_.wait_event(start)
         for i in range(B):
-            with torch.cuda.stream(s_in):
-                xd[i].copy_(xh[i], non_blocking=True)
-                up = torch.cuda.Event()
-                up.record(s_in)
-            s_cmp.wait_event(up)
-            with torch.cuda.stream(s_cmp):
-                C.causal_conv1d_fn(xd[i : i + 1].transpose(1, 2), w, bias, "silu",
-                                   out=yd[i : i + 1].transpose(1, 2))
-                done = torch.cuda.Event()
-                done.record(s_cmp)
-            s_out.wait_event(done)
-            with torch.cuda.stream(s_out):
-                oh[i].copy_(yd[i], non_blocking=True)
+            for k in range(E2E_CHUNKS):
+                t0, t1 = k * Lc, (k + 1) * Lc
+                with torch.cuda.stream(s_in):
+                    xd[i, t0:t1].copy_(xh[i, t0:t1], non_blocking=True)
+                    up = torch.cuda.Event()
+                    up.record(s_in)
+                s_cmp.wait_event(up)
+                with torch.cuda.stream(s_cmp):
+                    lo = max(t0 - (W - 1), 0)
+                    dst = yc[i, k, W - 1 - (t0 - lo):]
+                    C.causal_conv1d_fn(xd[i : i + 1, lo:t1].transpose(1, 2), w, bias, "silu",
+                                       out=dst.unsqueeze(0).transpose(1, 2))
+                    done = torch.cuda.Event()
+                    done.record(s_cmp)
+                s_out.wait_event(done)
+                with torch.cuda.stream(s_out):
+                    oh[i, t0:t1].copy_(yc[i, k, W - 1:], non_blocking=True)
         main.wait_stream(s_out)
 
     for _ in range(2):
