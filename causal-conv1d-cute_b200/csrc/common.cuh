@@ -292,10 +292,11 @@ __device__ __forceinline__ float activate(float a, bool use_silu) {
 }
 
 // State blocks: transpose between the channel-major state block (element e*SS + s of the block, V*SS
-// elements in SS vectors) and SS time-major vectors (vector s, lane e).
-template <typename T, int SS>
-__device__ __forceinline__ void block_to_time(const uint4 (&blk)[SS], uint4 (&tm)[SS]) {
-    constexpr int V = Vec<T>::V;
+// elements in SS vectors) and SS time-major vectors (vector s, lane e). R is the vector type
+// (uint4, or uint2 for the half-width kernels); V = sizeof(R) / sizeof(T).
+template <typename T, int SS, typename R>
+__device__ __forceinline__ void block_to_time(const R (&blk)[SS], R (&tm)[SS]) {
+    constexpr int V = (int)(sizeof(R) / sizeof(T));
 #pragma unroll
     for (int e = 0; e < V; ++e)
 #pragma unroll
@@ -305,9 +306,9 @@ __device__ __forceinline__ void block_to_time(const uint4 (&blk)[SS], uint4 (&tm
         }
 }
 
-template <typename T, int N>
-__device__ __forceinline__ void time_to_block(const uint4* tm, uint4 (&blk)[N]) {
-    constexpr int V = Vec<T>::V;
+template <typename T, int N, typename R>
+__device__ __forceinline__ void time_to_block(const R* tm, R (&blk)[N]) {
+    constexpr int V = (int)(sizeof(R) / sizeof(T));
 #pragma unroll
     for (int q = 0; q < N; ++q)
 #pragma unroll
@@ -389,16 +390,16 @@ __device__ __forceinline__ void load_filter(const T* __restrict__ weight, int64_
 // The same filter kept as raw storage-type vectors (W tap-major vectors wt[k], lane e = channel
 // c0 + e, plus the bias vector): a quarter of the registers of the fp32 form for bf16/fp16. Decode
 // kernels use each weight once per row, so widening at use costs nothing extra.
-template <typename T, int W>
+template <typename T, int W, typename R>
 __device__ __forceinline__ void load_filter_raw(const T* __restrict__ weight, int64_t w_sd,
                                                 int64_t w_sk, const T* __restrict__ bias,
                                                 int64_t bias_s, int64_t c0, bool wvec, bool bvec,
-                                                uint4 (&wt)[W], uint4& bt) {
-    constexpr int V = Vec<T>::V;
+                                                R (&wt)[W], R& bt) {
+    constexpr int V = (int)(sizeof(R) / sizeof(T));
     if (wvec) {
-        uint4 blk[W];
+        R blk[W];
 #pragma unroll
-        for (int q = 0; q < W; ++q) blk[q] = ldg16(weight + c0 * W + q * V);
+        for (int q = 0; q < W; ++q) blk[q] = __ldg(reinterpret_cast<const R*>(weight + c0 * W + q * V));
 #pragma unroll
         for (int e = 0; e < V; ++e)
 #pragma unroll
@@ -413,9 +414,9 @@ __device__ __forceinline__ void load_filter_raw(const T* __restrict__ weight, in
             for (int k = 0; k < W; ++k) set_lane<T>(wt[k], e, __ldg(weight + (c0 + e) * w_sd + k * w_sk));
     }
     if (bias == nullptr) {
-        bt = make_uint4(0, 0, 0, 0);
+        bt = R{};
     } else if (bvec) {
-        bt = ldg16(bias + c0);
+        bt = __ldg(reinterpret_cast<const R*>(bias + c0));
     } else {
 #pragma unroll
         for (int e = 0; e < V; ++e) set_lane<T>(bt, e, __ldg(bias + (c0 + e) * bias_s));

@@ -210,3 +210,38 @@ def test_single_sequence_with_padding_rows(rows, bos, eos, use_init):
     exp = st0.clone()
     exp[1] = full[:, -K:]
     assert torch.equal(st, exp)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("layout", [None, "dense", "dedup"])
+def test_update_vector_forms_agree(layout):
+    """160 rows of 8192 bf16 channels take the update kernel with 16-byte vectors (8 channels per
+    thread); the same call on the first 8 rows alone takes its half-width form (4 channels per
+    thread, used when a batch gives few threads). Outputs, states and per-step states of those
+    rows must agree bit for bit."""
+    B, D, W, L, n = 160, 8192, 4, 3, 8
+    K, slots = W - 1, B + 4
+    g = torch.Generator(device="cuda").manual_seed(11)
+    dt = torch.bfloat16
+    x = torch.randn(B, L, D, device="cuda", dtype=dt, generator=g).transpose(1, 2)
+    w = torch.randn(D, W, device="cuda", dtype=dt, generator=g)
+    b = torch.randn(D, device="cuda", dtype=dt, generator=g)
+    st0 = torch.randn(slots, D, K, device="cuda", dtype=dt, generator=g)
+    idx = torch.randperm(slots, device="cuda", generator=g)[:B].to(torch.int32)
+    st_full, st_part = st0.clone(), st0.clone()
+    phys_full, inter_full = _inter(layout, slots, L, D, K, dt)
+    phys_part, inter_part = _inter(layout, slots, L, D, K, dt)
+    y_full = causal_conv1d_update(x, st_full, w, b, "silu", idx, PAD, inter_full,
+                                  None if layout is None else idx)
+    y_part = causal_conv1d_update(x[:n], st_part, w, b, "silu", idx[:n], PAD, inter_part,
+                                  None if layout is None else idx[:n])
+    torch.cuda.synchronize()
+    rows = idx[:n].long()
+    assert torch.equal(y_full[:n], y_part)
+    assert torch.equal(st_full[rows], st_part[rows])
+    if layout is not None:
+        assert torch.equal(phys_full[rows], phys_part[rows])
+    ref_out, ref_st, _ = oracle.update(to_np(x[:n]), to_np(st0), to_np(w), to_np(b), True,
+                                       to_np(idx[:n]), PAD, None, None, "bf16")
+    assert_close(y_part, ref_out, dt)
+    assert_bits(st_part, ref_st)
