@@ -323,6 +323,19 @@ __device__ __forceinline__ void time_to_block(const R* tm, R (&blk)[N]) {
 // of kSlotCacheDevices zero-initialised ints owned by the caller; 0 when the query fails.
 constexpr int kSlotCacheDevices = 64;
 
+// Streaming multiprocessors of the current device (0 when the query fails), cached per device.
+inline int device_sm_count() {
+    static int cache[kSlotCacheDevices] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSlotCacheDevices) return 0;
+    if (cache[dev] == 0) {
+        int sms = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        cache[dev] = sms;
+    }
+    return cache[dev];
+}
+
 inline int device_slots(const void* kern, int threads, int* cache) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kSlotCacheDevices) return 0;

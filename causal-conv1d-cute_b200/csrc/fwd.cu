@@ -25,6 +25,7 @@ constexpr int kClThreads = 64;
 constexpr int kCfThreads = 256;
 constexpr int kCfElems = 16;  // elements per lane per iteration of the flat-stream kernel
 constexpr int kGenThreads = 256;
+constexpr int64_t kCfLongRow = 16384;  // see run_fwd's flat-stream launch
 
 template <typename T, int W, int U, bool PF, int NT>
 __global__ void __launch_bounds__(NT)
@@ -367,9 +368,16 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
         const bool v32 = host_aligned32(a.x) && host_aligned32(a.out);
         auto kern = v32 ? fwd_channel_first_kernel<T, W, true> : fwd_channel_first_kernel<T, W, false>;
         static int slot_cache[2][kSlotCacheDevices] = {};
-        const int64_t wave_warps =
-            std::max<int64_t>(1, device_slots((const void*)kern, kCfThreads, slot_cache[v32])) *
-            (kCfThreads / 32);
+        int64_t slots = std::max(1, device_slots((const void*)kern, kCfThreads, slot_cache[v32]));
+        // Rows of at least kCfLongRow elements: 3 resident CTAs per SM instead of 4. Measured on
+        // B200 (bf16, W = 4, 8192 channels; 4 -> 3 CTAs per SM): B = 1 with L = 20000, 30001,
+        // 36000, 40807, 45000, 50000, 57011, 65536: -8.9, -9.4, -10.6, -9.2, -10.8, -14.5, -10.7,
+        // -9.7 %; B = 2, L = 16384: -7.5 %; but B = 4, L = 8192: +0.9 %; B = 16, L = 2048: +0.4 %;
+        // B = 8, L = 4096 / 7000: +5.1 / +3.9 %; B = 6, L = 5000: +5.5 %. (Wider filters need
+        // more registers and run at 3 CTAs per SM already.)
+        const int sms = device_sm_count();
+        if (a.L >= kCfLongRow && sms > 0 && slots >= 4LL * sms) slots = 3LL * sms;
+        const int64_t wave_warps = slots * (kCfThreads / 32);
         const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
         const int64_t warps = ceil_div(chunks, iters);
         const int64_t blocks = ceil_div(warps * 32, kCfThreads);
