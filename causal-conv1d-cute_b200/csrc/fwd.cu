@@ -25,7 +25,6 @@ constexpr int kClThreads = 64;
 constexpr int kCfThreads = 256;
 constexpr int kCfElems = 16;  // elements per lane per iteration of the flat-stream kernel
 constexpr int kGenThreads = 256;
-constexpr int64_t kCfLongRow = 16384;  // see run_fwd's flat-stream launch
 
 template <typename T, int W, int U, bool PF, int NT>
 __global__ void __launch_bounds__(NT)
@@ -173,8 +172,15 @@ __global__ void __launch_bounds__(kCfThreads)
                 wc = c;
             }
             float o[EPT];
-            if (full && t >= K && t + EPT <= L) {
-                // Fast path: the elements and their W-1 predecessors lie in one row.
+            if (full && t + EPT <= L) {
+                // Fast path: the elements lie in one row. At a row start (t < W-1) the window
+                // entries before the row are zeroed, which is the slow path's causal padding (a
+                // zero tap still goes through the same fused multiply-add, so the bits agree).
+                if (t < K) {
+#pragma unroll
+                    for (int i = 0; i < K; ++i)
+                        if (i < K - t) win[i] = 0.f;
+                }
 #pragma unroll
                 for (int e = 0; e < EPT; ++e) {
                     float acc = b0;
@@ -369,14 +375,13 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
         auto kern = v32 ? fwd_channel_first_kernel<T, W, true> : fwd_channel_first_kernel<T, W, false>;
         static int slot_cache[2][kSlotCacheDevices] = {};
         int64_t slots = std::max(1, device_slots((const void*)kern, kCfThreads, slot_cache[v32]));
-        // Rows of at least kCfLongRow elements: 3 resident CTAs per SM instead of 4. Measured on
-        // B200 (bf16, W = 4, 8192 channels; 4 -> 3 CTAs per SM): B = 1 with L = 20000, 30001,
-        // 36000, 40807, 45000, 50000, 57011, 65536: -8.9, -9.4, -10.6, -9.2, -10.8, -14.5, -10.7,
-        // -9.7 %; B = 2, L = 16384: -7.5 %; but B = 4, L = 8192: +0.9 %; B = 16, L = 2048: +0.4 %;
-        // B = 8, L = 4096 / 7000: +5.1 / +3.9 %; B = 6, L = 5000: +5.5 %. (Wider filters need
-        // more registers and run at 3 CTAs per SM already.)
+        // At most 3 resident CTAs per SM (the 16-bit kernels for W <= 4 fit 4). Measured on B200
+        // (bf16, W = 4, 8192 channels; 4 -> 3 CTAs per SM, us): B x L = 1 x 20000: 126.8 -> 113.5;
+        // 1 x 40807: 243.6 -> 221.4; 1 x 65536: 381.5 -> 345.9; 8 x 4096: 199.1 -> 179.6;
+        // 4 x 8192: 198.7 -> 179.1; 16 x 2048: 193.5 -> 179.2; 2 x 16384: 197.2 -> 178.0;
+        // 8 x 7000: 314.8 -> 302.2; 6 x 5000: 165.8 -> 169.7 (the one shape of 14 that lost).
         const int sms = device_sm_count();
-        if (a.L >= kCfLongRow && sms > 0 && slots >= 4LL * sms) slots = 3LL * sms;
+        if (sms > 0 && slots > 3LL * sms) slots = 3LL * sms;
         const int64_t wave_warps = slots * (kCfThreads / 32);
         const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
         const int64_t warps = ceil_div(chunks, iters);
