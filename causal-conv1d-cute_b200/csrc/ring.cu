@@ -159,10 +159,17 @@ __global__ void __launch_bounds__(kRingThreads) ring_convert_kernel(const RingCo
             st16(rp + r * a.r_sk, tm[k]);
         }
     } else {
+        // All K ring rows are read whatever the position, so the loads do not wait for `seen`;
+        // the rotation to oldest-first order is done in registers.
+        uint4 rows[K];
+#pragma unroll
+        for (int r = 0; r < K; ++r) rows[r] = ld16(rp + r * a.r_sk);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
             const int r = pos + k >= K ? pos + k - K : pos + k;
-            tm[k] = ld16(rp + r * a.r_sk);
+            tm[k] = rows[0];
+#pragma unroll
+            for (int q = 1; q < K; ++q) tm[k] = r == q ? rows[q] : tm[k];
         }
         time_to_block<T, K>(tm, blk);
 #pragma unroll
