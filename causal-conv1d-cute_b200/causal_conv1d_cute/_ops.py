@@ -1,5 +1,6 @@
 """Tensor-level calls into libcc1d.so, registered as torch.library ops (cc1d::fwd, cc1d::update,
-cc1d::update_ring, cc1d::varlen, cc1d::update_unpack, cc1d::fwd_states, cc1d::ring_convert).
+cc1d::update_ring, cc1d::varlen, cc1d::update_unpack, cc1d::fwd_states, cc1d::to_ring,
+cc1d::from_ring).
 
 Each op passes data pointers, element strides and sizes of already-validated CUDA tensors to
 one C entry point, on the current stream of the tensors' device. No host synchronisation, no
@@ -150,16 +151,23 @@ def _update_ring_impl(x, ring, weight, bias, silu, out, seen, idx, pad):
     return out
 
 
-def _ring_convert_impl(to_ring, state, ring, seen):
-    """Ordered state (slots, dim, W-1) <-> ring state (slots, W-1, dim) (cc1d_to_ring /
-    cc1d_from_ring); seen is an int32 CUDA tensor (slots,)."""
+def _to_ring_impl(state, ring, seen):
+    """Ordered state (slots, dim, W-1) -> ring state (slots, W-1, dim) (cc1d_to_ring); seen is an
+    int32 CUDA tensor (slots,)."""
     lib = load()
     S, D, K = state.shape
-    args = (state.data_ptr(), *state.stride(), ring.data_ptr(), *ring.stride())
-    if not to_ring:
-        args = (ring.data_ptr(), *ring.stride(), state.data_ptr(), *state.stride())
-    f = lib.cc1d_to_ring if to_ring else lib.cc1d_from_ring
-    check(f(*args, seen.data_ptr(), S, D, K + 1, dtype_code(state.dtype), _stream(state.device)))
+    check(lib.cc1d_to_ring(state.data_ptr(), *state.stride(), ring.data_ptr(), *ring.stride(),
+                           seen.data_ptr(), S, D, K + 1, dtype_code(state.dtype),
+                           _stream(state.device)))
+
+
+def _from_ring_impl(ring, state, seen):
+    """Ring state (slots, W-1, dim) -> ordered state (slots, dim, W-1) (cc1d_from_ring)."""
+    lib = load()
+    S, D, K = state.shape
+    check(lib.cc1d_from_ring(ring.data_ptr(), *ring.stride(), state.data_ptr(), *state.stride(),
+                             seen.data_ptr(), S, D, K + 1, dtype_code(state.dtype),
+                             _stream(state.device)))
 
 
 def _varlen_impl(x, weight, bias, silu, out, qsl, cidx, hinit, states, pad):
@@ -229,7 +237,8 @@ _SCHEMAS = {
         "update_ring(Tensor x, Tensor(a!) ring, Tensor weight, Tensor? bias, bool silu, "
         "Tensor(b!) out, Tensor seen, Tensor? idx, int pad) -> ()"
     ),
-    "ring_convert": "ring_convert(bool to_ring, Tensor(a!) state, Tensor(b!) ring, Tensor seen) -> ()",
+    "to_ring": "to_ring(Tensor state, Tensor(a!) ring, Tensor seen) -> ()",
+    "from_ring": "from_ring(Tensor ring, Tensor(a!) state, Tensor seen) -> ()",
     "varlen": (
         "varlen(Tensor x, Tensor weight, Tensor? bias, bool silu, Tensor(a!) out, Tensor qsl, "
         "Tensor? cidx, Tensor? hinit, Tensor(b!)? states, int pad) -> ()"
@@ -242,7 +251,8 @@ _SCHEMAS = {
 }
 _IMPLS = {
     "fwd": _fwd_impl, "fwd_states": _fwd_states_impl, "update": _update_impl,
-    "update_ring": _update_ring_impl, "ring_convert": _ring_convert_impl, "varlen": _varlen_impl,
+    "update_ring": _update_ring_impl, "to_ring": _to_ring_impl, "from_ring": _from_ring_impl,
+    "varlen": _varlen_impl,
     "update_unpack": _update_unpack_impl,
 }
 
@@ -300,9 +310,14 @@ def update_ring(x, ring, weight, bias, silu, out, seen, idx, pad):
     return out
 
 
-def ring_convert(to_ring, state, ring, seen):
-    """Ordered state <-> ring state (op cc1d::ring_convert)."""
-    _op.ring_convert(bool(to_ring), state, ring, seen)
+def to_ring(state, ring, seen):
+    """Ordered state -> ring state; writes only `ring` (op cc1d::to_ring)."""
+    _op.to_ring(state, ring, seen)
+
+
+def from_ring(ring, state, seen):
+    """Ring state -> ordered state; writes only `state` (op cc1d::from_ring)."""
+    _op.from_ring(ring, state, seen)
 
 
 def varlen(x, weight, bias, silu, out, qsl, cidx, hinit, states, pad):
@@ -319,6 +334,6 @@ def update_unpack(qkvz, ba, state, weight, bias, out, z, b, a, idx, heads, silu,
 
 
 __all__ = [
-    "device_status", "fwd", "fwd_states", "ring_convert", "set_device_checks", "update", "update_ring", "update_unpack",
+    "device_status", "from_ring", "fwd", "fwd_states", "to_ring", "set_device_checks", "update", "update_ring", "update_unpack",
     "varlen", "_lib",
 ]

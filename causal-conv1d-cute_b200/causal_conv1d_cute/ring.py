@@ -44,7 +44,7 @@ def to_ring(conv_state, cache_seqlens):
     if not 1 <= K <= 7:
         _unsupported(f"state length {K} is outside 1..7")
     ring = torch.empty((S, K, D), dtype=conv_state.dtype, device=conv_state.device)
-    _ops.ring_convert(True, conv_state, ring, seen)
+    _ops.to_ring(conv_state, ring, seen)
     return ring
 
 
@@ -59,5 +59,5 @@ def from_ring(ring_state, cache_seqlens):
     if not 1 <= K <= 7:
         _unsupported(f"state length {K} is outside 1..7")
     state = torch.empty((S, D, K), dtype=ring_state.dtype, device=ring_state.device)
-    _ops.ring_convert(False, state, ring_state, seen)
+    _ops.from_ring(ring_state, state, seen)
     return state

@@ -109,3 +109,105 @@ def check(case: Case, t, got, ref32):
     if not bwd_err <= bound:
         return ("WRONG", ulp_err, bwd_err)
     return ("ok" if ulp_err <= 1.5 else "lowprec", ulp_err, bwd_err)
+
+
+# ---------------------------------------------------------------------------------------------
+# fp32 references of every entry point, computed with PyTorch on the tensors' own device. They
+# extend reference() above (reference testing.py:105-128) to the packed, multi-step, indexed and
+# ring paths, following the reference's CPU algorithm (fallback.py:49-164, functional.py:911-922):
+# an unrounded fp32 output for the accuracy check and the cache writes, which are copies of the
+# inputs, exactly. bench.py gates every timed path on them, and the tests use them over whole
+# BASELINE-sized tensors. Outputs of skipped rows (pad slots, empty sequences) are NaN.
+# ---------------------------------------------------------------------------------------------
+
+
+def _conv_hist(full, w, b, silu):
+    """Valid depthwise conv of full (..., D, n + W - 1) in fp32 -> (..., D, n)."""
+    D, W = w.shape
+    lead = full.shape[:-2]
+    y = F.conv1d(full.float().reshape(-1, D, full.shape[-1]), w.float().unsqueeze(1),
+                 None if b is None else b.float(), groups=D)
+    y = y.reshape(*lead, D, y.shape[-1])
+    return F.silu(y) if silu else y
+
+
+def ref_fwd(x, w, b, silu):
+    """Prefill (batch, dim, seqlen) -> fp32 output with zero history before every row."""
+    W = w.shape[1]
+    return _conv_hist(F.pad(x.float(), (W - 1, 0)), w, b, silu)
+
+
+def ref_varlen(x, w, b, qsl, cidx, hinit, states, silu, pad=-1):
+    """Packed prefill of x (dim, ntokens) -> (fp32 output, states after) (fallback.py:77-114).
+
+    states (slots, dim, W-1) is not modified; a copy with every live sequence's final state is
+    returned (None without states)."""
+    D, T = x.shape
+    K = w.shape[1] - 1
+    out = torch.full((D, T), float("nan"), device=x.device)
+    st = None if states is None else states.clone()
+    bounds = [int(v) for v in qsl.tolist()]
+    slots = list(range(len(bounds) - 1)) if cidx is None else [int(v) for v in cidx.tolist()]
+    init = [False] * len(slots) if hinit is None else [bool(v) for v in hinit.tolist()]
+    for i, slot in enumerate(slots):
+        a, e = bounds[i], bounds[i + 1]
+        if e <= a or (st is not None and slot == pad):
+            continue
+        h = st[slot] if st is not None and init[i] else x.new_zeros(D, K)
+        full = torch.cat([h, x[:, a:e]], dim=1)
+        out[:, a:e] = _conv_hist(full, w, b, silu)
+        if st is not None:
+            st[slot] = full[:, full.shape[1] - K:]
+    return out, st
+
+
+def ref_update(x, state, w, b, silu, idx=None, pad=-1, inter=None, iidx=None):
+    """Decode of x (batch, dim) or (batch, dim, steps) against state (slots, dim, S >= W-1) ->
+    (fp32 output, state after, dense per-step windows after) (fallback.py:117-164). Pad rows keep
+    their state; the inputs are not modified."""
+    W = w.shape[1]
+    K = W - 1
+    xs = x.unsqueeze(-1) if x.dim() == 2 else x
+    B, D, L = xs.shape
+    slots = torch.arange(B, device=x.device) if idx is None else idx.long()
+    live = slots != pad
+    st = state.clone()
+    it = None if inter is None else inter.clone()
+    full = torch.cat([state[slots.clamp_min(0)], xs], dim=-1)  # (B, D, S + L)
+    out = _conv_hist(full[..., full.shape[-1] - (K + L):], w, b, silu)
+    out[~live] = float("nan")
+    st[slots[live]] = full[live][..., L:]
+    if it is not None:
+        islots = slots if iidx is None else iidx.long()
+        S = state.shape[-1]
+        for t in range(L):
+            first = S + t + 1 - K
+            it[islots[live], t] = full[live][..., first:first + K]
+    return (out[..., 0] if x.dim() == 2 else out), st, it
+
+
+def ref_update_ring(x, ring, w, b, silu, seen, idx=None, pad=-1):
+    """Single-token decode on a ring state (slots, W-1, dim) -> (fp32 output, ring after):
+    from_ring + update + overwrite of row seen % (W-1) (functional.py:911-922)."""
+    K = ring.shape[1]
+    B, D = x.shape
+    slots = torch.arange(B, device=x.device) if idx is None else idx.long()
+    live = slots != pad
+    rows = (seen.long().unsqueeze(1) + torch.arange(K, device=x.device)) % K  # (B, K)
+    sl = slots.clamp_min(0)
+    ordered = ring[sl.unsqueeze(1), rows]  # (B, K, D), oldest first
+    full = torch.cat([ordered.transpose(1, 2), x.unsqueeze(-1)], dim=-1)
+    out = _conv_hist(full, w, b, silu)[..., 0]
+    out[~live] = float("nan")
+    rg = ring.clone()
+    pos = seen.long() % K
+    rg[slots[live], pos[live]] = x[live]
+    return out, rg
+
+
+def within(got, ref, tol):
+    """|got - ref| <= tol + tol |ref| wherever ref is not NaN (NaN marks undefined outputs)."""
+    got, ref = got.float(), ref.float()
+    keep = ~torch.isnan(ref)
+    err = (got - ref).abs()
+    return bool(((err <= tol + tol * ref.abs()) | ~keep).all())

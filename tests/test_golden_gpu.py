@@ -96,3 +96,26 @@ def test_ring_convert():
     r = C.to_ring(_t(a, "state"), _t(a, "seen"))
     assert_bits(r, a["ring"])
     assert_bits(C.from_ring(r, _t(a, "seen")), a["back"])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", names("unpack_"))
+def test_update_unpack(name):
+    """Fused decode+unpack against the reference's own GPU kernel's outputs."""
+    from causal_conv1d_cute import unpack
+
+    meta, a = load(name)
+    q = _t(a, "qkvz")
+    B, cols = q.shape
+    wide = torch.zeros(B, cols + meta["row_extra"], device="cuda", dtype=q.dtype)
+    wide[:, :cols] = q
+    qkvz = wide[:, :cols]
+    st = _t(a, "state0")
+    out, z, b, ga = unpack.causal_conv1d_update_unpack(qkvz, _t(a, "ba"), st, _t(a, "w"),
+                                                       _t(a, "bias"), _t(a, "idx"), meta["heads"],
+                                                       meta["act"], meta["pad"])
+    assert_close(out, a["out"], q.dtype)
+    assert_bits(z, a["z"])
+    assert_bits(b, a["b"])
+    assert_bits(ga, a["a"])
+    assert_bits(st, a["state"])

@@ -114,3 +114,19 @@ def test_round_to_matches_numpy_f16_and_bf16_ties():
     # is a tie between 1 + 2^-7 and 1 + 2^-6 and rounds to the even 1 + 2^-6.
     r = oracle.round_to(x[:3], "bf16")
     assert r.tolist() == [1.0, 1.0, 1.015625]
+
+
+@pytest.mark.parametrize("name", names("unpack_"))
+def test_unpack_golden(name):
+    """The fused decode+unpack vectors come from the reference's GPU kernel (ConvUpdateUnpack,
+    unpack.py:33-222; tests/golden/make_golden_unpack.py), its only implementation."""
+    meta, a = load(name)
+    dt = a.dtypes["qkvz"]
+    out, z, b, ga, st = oracle.update_unpack(a["qkvz"], a["ba"], a["state0"], a["w"], a.get("bias"),
+                                             a["idx"], meta["heads"], meta["act"] is not None,
+                                             meta["pad"], dt)
+    _close(out, a["out"], dt)
+    _bits_equal(z, a["z"])
+    _bits_equal(b, a["b"])
+    _bits_equal(ga, a["a"])
+    _bits_equal(st, a["state"])

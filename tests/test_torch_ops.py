@@ -15,7 +15,8 @@ MUTATED = {
     "fwd_states": {"out", "final_states"},
     "update": {"state", "out3", "inter"},
     "update_ring": {"ring", "out"},
-    "ring_convert": {"state", "ring"},
+    "to_ring": {"ring"},
+    "from_ring": {"state"},
     "varlen": {"out", "states"},
     "update_unpack": {"state", "out", "z", "b", "a"},
 }
