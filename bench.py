@@ -2,32 +2,48 @@
 """Benchmark of the depthwise causal conv1d hot path on B200.
 
 python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-paths]
-python bench.py --profile fwd|decode|ring|spec|varlen   (4 launches of one kernel, for ncu)
+                [--no-reference-cute]
+python bench.py --profile CASE [--width W]   (a few launches of one kernel, for ncu)
 
 Headline (the configuration the metric is quoted on): prefill of
 x (batch 8, seqlen 4096, dim 8192) bf16 ~N(0,1) stored token-major and passed as its
 (batch, dim, seqlen) view, weight (8192, 4) ~U(-0.5, 0.5), bias ~N(0, 0.1), SiLU. One step is one
 causal_conv1d_fn call over that batch. value = algorithmic bytes (every input element read once,
-every output element written once, plus weights and bias) / device time, summed over ranks.
-Inputs (512 MiB) exceed L2 (126 MB), so no flush is needed between steps. e2e is the same
-metric with the input in pinned host memory and the result read back to it inside every step:
-the public causal_conv1d_fn is called once per 1024-token chunk of each batch row (over a window
-that starts W - 1 tokens earlier, so each output has its full history), and chunks are pipelined
-over three streams (upload of chunk i + 1, convolution of chunk i, download of chunk i - 1).
+every output element written once, plus weights and bias) / device time of all steps. Inputs
+(512 MiB) exceed L2 (126 MB), so no flush is needed between steps. Before timing, the output of
+one step is compared with the fp32 PyTorch reference on every element ("parity").
+e2e is the same metric with the input in pinned host memory and the result read back to it inside
+every step: the public causal_conv1d_fn is called once per 1024-token chunk of each batch row
+(over a window that starts W - 1 tokens earlier, so each output has its full history), and chunks
+are pipelined over three streams (upload of chunk i + 1, convolution of chunk i, download of
+chunk i - 1).
 
-At N > 1 (torchrun, one rank per GPU) the layer is channel-sliced as tensor parallelism shards it:
-rank r owns channels [8192 r, 8192 (r + 1)) of a layer with 8192 N channels, so per-GPU work is
-fixed (weak scaling) and the kernels exchange nothing. NCCL is used once, after timing, to
-all-gather a sample of every rank's outputs and compare them bit for bit with the unsharded run.
+At N > 1 (torchrun, one rank per GPU) the layer is channel-sliced as tensor parallelism shards it
+(strong scaling): rank r owns channels [r D/N, (r + 1) D/N) of config 2's D = 8192 as its own
+contiguous (8, 4096, D/N) activation, and the kernels exchange nothing. value = the whole layer's
+bytes / the slowest rank's time. After timing, NCCL all-gathers every rank's whole output (and,
+for the decode and varlen paths, its whole state cache) and rank 0 compares them bit for bit with
+the unsharded run (causal_conv1d_cute.shard.sharded_equals_unsharded). Config 3 (decode) and
+config 5 (varlen, W = 4) are timed sharded too ("sharded").
 
-With N = 1 the other BASELINE paths are measured too ("paths"): config 2 stored channel-first,
-config 2 with initial and final states and with sequence ids (the Dao-interface extras), indexed
-decode (config 3) and its ring variant with the to_ring / from_ring conversions, direct-state
-decode at B = 256 and 64 and ring decode at B = 64 (the shapes of the reference's published
-decode numbers), the 4-step speculative verify with dense per-step states (config 4), and packed
-varlen prefill (config 5) at widths 2, 3, 4 and 8, token-major and channel-first, each replayed in
-a CUDA graph (no host launch gaps). Decode inputs fit in L2, so "cold" cycles 8 independent input sets whose total
-exceeds L2, and "warm" repeats one set.
+With N = 1 the other BASELINE paths are measured too ("paths"), each after its own parity check
+against the fp32 PyTorch reference (outputs within 1e-2, cache writes bit for bit; a WRONG path
+is not timed): config 2 stored channel-first and at widths 2 and 8, config 2 with initial and
+final states and with sequence ids (the Dao-interface extras), decode (config 3), ring decode
+(config 3r) with the to_ring / from_ring conversions, the reference's published decode shapes
+(direct state at B = 256 and 64, ring at B = 64), the 4-step speculative verify with dense
+per-step states (config 4), the fused Gated DeltaNet decode at the reference's sglang shape, and
+packed varlen prefill (config 5) at widths 2, 3, 4 and 8, token-major and channel-first. Decode
+paths run inside CUDA graphs: "us_cold" = (graph of n x [256 MiB L2 flush, call] - graph of
+n x [flush]) / n, the reference's cold-L2 protocol; "us_warm" = graph of n back-to-back calls / n.
+Prefill and varlen inputs exceed L2: "us" = replays of a one-call graph.
+"copy_ceiling" is the library's own 32-byte-vector D2D copy (cc1d_copy) of the headline's bytes.
+
+"reference_cute" runs the same paths through the reference package's own public API and CuTe DSL
+kernels (baseline/_ref, unmodified) on the same GPU with the same timers, in a child process. The
+image's nvidia-cutlass-dsl is 4.5.0 and the reference requires >= 4.6: the one difference that
+matters, cute.math.tanh(approx=True) (4.6) spelled cute.math.tanh(fastmath=True) in 4.5.0, is
+bridged by forwarding that keyword before the reference is imported; nothing else is changed.
 
 --impl reference times the reference's CPU algorithm (the C port of its PyTorch fallback,
 oracle/cc1d_oracle.c) on the host cores, on bounded samples of the same workload.
@@ -35,16 +51,19 @@ oracle/cc1d_oracle.c) on the host cores, on bounded samples of the same workload
 
 import argparse
 import json
-import math
 import os
 import statistics
+import subprocess
 import sys
 import threading
 import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-for p in (str(ROOT / "causal-conv1d-cute_b200"), str(ROOT)):
+PKG = ROOT / "causal-conv1d-cute_b200"
+REF_PKG = ROOT / "baseline" / "_ref"
+REF_CHILD = "--reference-cute-child" in sys.argv
+for p in ((str(REF_PKG), str(ROOT)) if REF_CHILD else (str(PKG), str(ROOT))):
     if p not in sys.path:
         sys.path.insert(0, p)
 
@@ -57,22 +76,24 @@ E = 2  # bf16
 HEADLINE_BYTES = 2 * B * L * D * E + D * W * E + D * E  # 1,073,823,744
 # The kernel the headline call dispatches to (balanced shares: W = 4, 4096-token sequences).
 HEADLINE_KERNEL = "fwd_channel_last_share_kernel"
-L2_BYTES = 126 * 2**20
+FLUSH_BYTES = 256 * 2**20  # twice L2 (126 MB)
 E2E_CHUNKS = 4  # token chunks per batch row in the e2e pipeline
+TOL = 1e-2  # bf16 output tolerance (atol = rtol)
+BF = torch.bfloat16
 
 
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=2000)
-    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=("ours", "reference"), default="ours")
     p.add_argument("--no-paths", action="store_true")
-    p.add_argument("--profile", choices=("fwd", "fwd_cf", "decode", "ring", "spec", "varlen", "varlen_cf"),
-                   default=None,
-                   help="run 4 launches of one kernel on a case larger than L2 (for ncu) and exit")
-    p.add_argument("--width", type=int, default=W,
-                   help="filter width of the --profile case (prefill and varlen cases)")
+    p.add_argument("--no-reference-cute", action="store_true")
+    p.add_argument("--reference-cute-child", action="store_true", help=argparse.SUPPRESS)
+    p.add_argument("--profile", default=None, choices=sorted(PROFILE_CASES),
+                   help="run a few launches of one kernel on a case larger than L2 (for ncu), exit")
+    p.add_argument("--width", type=int, default=W, help="filter width of the --profile case")
     return p.parse_args()
 
 
@@ -102,7 +123,8 @@ def profiled_traffic(kernel):
 
 
 class ClockSampler:
-    """Samples SM clock and clock-event reasons through NVML on a background thread."""
+    """Samples SM clock and clock-event reasons through NVML on a background thread, as fast as
+    NVML answers (period 0.5 ms), so that even a few-millisecond timed region gets samples."""
 
     REASONS = {
         "hw_slowdown": 0x8,
@@ -112,7 +134,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index, period=0.01):
+    def __init__(self, device_index, period=0.0005):
         self.samples = []
         self.period = period
         self._stop = threading.Event()
@@ -183,17 +205,14 @@ class ClockSampler:
 # ---------------------------------------------------------------------------------------------
 
 
-def time_launches(step, steps, flush=None):
+def time_launches(step, steps):
     """Run `step` `steps` times on the current stream; return (total ms, per-launch ms list).
 
-    Each launch is bracketed by its own CUDA events (so a cold-L2 flush issued between launches is
-    not counted); the total spans the first start to the last end.
-    """
+    Each launch is bracketed by its own CUDA events; the total spans the first start to the last
+    end (so it also counts any gap between launches)."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
-        if flush is not None:
-            flush()
         starts[i].record()
         step()
         ends[i].record()
@@ -202,29 +221,461 @@ def time_launches(step, steps, flush=None):
     return starts[0].elapsed_time(ends[-1]), per
 
 
+def capture(calls):
+    """A CUDA graph of `calls` run back to back (warmed up once on a side stream first)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for f in calls:
+            f()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for f in calls:
+            f()
+    graph.replay()
+    torch.cuda.synchronize()
+    return graph
+
+
+def replay_ms(graph, reps=1):
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / reps
+
+
+class Flusher:
+    """Writes FLUSH_BYTES (twice L2) so that the next kernel finds nothing of its data in L2."""
+
+    def __init__(self, device):
+        self.buf = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    def __call__(self):
+        self.buf.fill_(1)
+
+
+def cold_warm_us(call, flush, n=20, rounds=5):
+    """Per-call microseconds of a decode-sized call: cold (L2 flushed before every call) and warm.
+
+    cold = (graph of n x [flush, call] - graph of n x [flush]) / n, median over rounds: the call's
+    device time after a flush, including the graph's gap before it, without the flush itself.
+    warm = graph of n back-to-back calls / n."""
+    g_fc = capture([flush, call] * n)
+    g_f = capture([flush] * n)
+    g_c = capture([call] * n)
+    cold, warm = [], []
+    for _ in range(rounds):
+        tf = replay_ms(g_f)
+        tfc = replay_ms(g_fc)
+        cold.append((tfc - tf) * 1e3 / n)
+        warm.append(replay_ms(g_c) * 1e3 / n)
+    del g_fc, g_f, g_c
+    return statistics.median(cold), statistics.median(warm)
+
+
+def big_us(call, reps=20):
+    """Per-call microseconds of a call whose inputs exceed L2: replays of a one-call graph."""
+    g = capture([call])
+    us = replay_ms(g, reps) * 1e3
+    del g
+    return us
+
+
 # ---------------------------------------------------------------------------------------------
-# Headline: prefill config 2
+# The BASELINE paths, written against the public API shared by this library and the reference
+# package (R), so that both arms run the same calls on the same inputs.
 # ---------------------------------------------------------------------------------------------
 
 
-def make_prefill(device, seed):
-    g = torch.Generator(device=device).manual_seed(seed)
-    x = torch.randn(B, L, D, device=device, dtype=torch.bfloat16, generator=g)
-    w = (torch.rand(D, W, device=device, generator=g) - 0.5).to(torch.bfloat16)
-    b = (torch.randn(D, device=device, generator=g) * 0.1).to(torch.bfloat16)
-    return x, w, b
+def _w(g, dim, width, dev):
+    return (torch.rand(dim, width, device=dev, generator=g) - 0.5).to(BF)
+
+
+def _b(g, dim, dev):
+    return (torch.randn(dim, device=dev, generator=g) * 0.1).to(BF)
+
+
+def _rows_within(y, x, w, b, T):
+    """Prefill output y (batch, dim, seqlen) against the fp32 reference, one batch row at a time."""
+    return all(T.within(y[i], T.ref_fwd(x[i:i + 1], w, b, True)[0], TOL) for i in range(y.shape[0]))
+
+
+def varlen_batch(dev, g, dim=D, nseq=32, seed=0):
+    """Config 5: nseq lengths ~ lognormal(7, 1) clipped to [1, 8192], 32 distinct slots of 512,
+    has_initial_state ~ Bernoulli(0.5); token-major x (T, dim)."""
+    rng = np.random.default_rng(seed)
+    lens = np.clip(np.round(rng.lognormal(7, 1, nseq)), 1, 8192).astype(np.int64)
+    T_ = int(lens.sum())
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=dev, dtype=torch.int32)
+    cidx = torch.from_numpy(rng.choice(512, nseq, replace=False).astype(np.int32)).to(dev)
+    hinit = torch.from_numpy(rng.random(nseq) < 0.5).to(dev)
+    xv = torch.randn(T_, dim, device=dev, generator=g).to(BF)
+    return T_, qsl, cidx, hinit, xv
+
+
+def varlen_bytes(dim, T_, width, hinit, nseq=32):
+    nh = int(hinit.sum())
+    return 2 * dim * T_ * E + dim * (width - 1) * E * (nseq + nh) + 4 * (nseq + 1) + 4 * nseq + nseq \
+        + dim * width * E
+
+
+def decode_bytes(Bq, dim, steps=1, width=4, idx=False, inter=False):
+    b = 2 * Bq * dim * steps * E + 2 * Bq * dim * (width - 1) * E + dim * width * E + dim * E
+    if idx:
+        b += Bq * 4
+    if inter:
+        b += Bq * steps * dim * (width - 1) * E + Bq * 4
+    return b
+
+
+def path_specs(R, T, dev, ours):
+    """(name, kind, nbytes, setup) for every path; setup() -> (call, check). kind "decode" is timed
+    cold and warm, "big" by graph replay. check() runs the call on copies of the inputs and
+    returns True when it matches the fp32 reference (outputs within TOL, caches bit for bit)."""
+    g = torch.Generator(device=dev).manual_seed(7)
+    specs = []
+    w4, b4 = _w(g, D, 4, dev), _b(g, D, dev)
+
+    def prefill_cf():
+        x = torch.randn(B, D, L, device=dev, generator=g).to(BF)
+        out = torch.empty_like(x)
+        return (lambda: R.causal_conv1d_fn(x, w4, b4, "silu", out=out),
+                lambda: _rows_within(R.causal_conv1d_fn(x, w4, b4, "silu"), x, w4, b4, T))
+
+    specs.append(("prefill_channel_first", "big", HEADLINE_BYTES, prefill_cf))
+
+    for Wv in (2, 8):
+        def prefill_w(Wv=Wv):
+            x = torch.randn(B, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
+            wv = _w(g, D, Wv, dev)
+            out = torch.empty(B, L, D, device=dev, dtype=BF).transpose(1, 2)
+            return (lambda: R.causal_conv1d_fn(x, wv, b4, "silu", out=out),
+                    lambda: _rows_within(R.causal_conv1d_fn(x, wv, b4, "silu"), x, wv, b4, T))
+
+        specs.append((f"prefill_w{Wv}", "big", 2 * B * L * D * E + D * Wv * E + D * E, prefill_w))
+
+    if ours:
+        def prefill_states():
+            x = torch.randn(B, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
+            init = torch.randn(B, 3, D, device=dev, generator=g).to(BF).transpose(1, 2)
+            fin = torch.empty_like(init)
+
+            def check():
+                y, f = R.causal_conv1d_fwd_states(x, w4, b4, None, init, True, None, "silu")
+                ok = True
+                for i in range(B):
+                    full = torch.cat([init[i:i + 1], x[i:i + 1]], dim=2)
+                    ref = T._conv_hist(full, w4, b4, True)[0]
+                    ok &= T.within(y[i], ref, TOL) and torch.equal(f[i], full[0, :, -3:])
+                return ok
+
+            return (lambda: R.causal_conv1d_fwd_states(x, w4, b4, None, init, True, fin, "silu"),
+                    check)
+
+        specs.append(("prefill_states", "big", HEADLINE_BYTES + 2 * B * D * 3 * E, prefill_states))
+
+        def prefill_seq():
+            x = torch.randn(B, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
+            seq = torch.zeros(B, L, device=dev, dtype=torch.int32)
+            seq[:, L // 2:] = 1
+
+            def check():
+                y = R.causal_conv1d_fwd_states(x, w4, b4, seq, None, False, None, "silu")
+                y = y[0] if isinstance(y, tuple) else y
+                ok = True
+                for i in range(B):
+                    for a, e in ((0, L // 2), (L // 2, L)):
+                        ref = T.ref_fwd(x[i:i + 1, :, a:e], w4, b4, True)[0]
+                        ok &= T.within(y[i, :, a:e], ref, TOL)
+                return ok
+
+            return (lambda: R.causal_conv1d_fwd_states(x, w4, b4, seq, None, False, None, "silu"),
+                    check)
+
+        specs.append(("prefill_seq_idx", "big", HEADLINE_BYTES + B * L * 4, prefill_seq))
+
+    def decode(Bq, slots, indexed):
+        def setup():
+            x = torch.randn(Bq, D, device=dev, generator=g).to(BF)
+            cache = torch.randn(slots, D, 3, device=dev, generator=g).to(BF)
+            idx = (torch.randperm(slots, device=dev, generator=g)[:Bq].to(torch.int32)
+                   if indexed else None)
+
+            def check():
+                c = cache.clone()
+                y = R.causal_conv1d_update(x, c, w4, b4, "silu", idx)
+                r_out, r_st, _ = T.ref_update(x, cache, w4, b4, True, idx)
+                return T.within(y, r_out, TOL) and torch.equal(c, r_st)
+
+            return lambda: R.causal_conv1d_update(x, cache, w4, b4, "silu", idx), check
+
+        return setup
+
+    specs.append(("decode_indexed_b256", "decode", decode_bytes(256, D, idx=True), decode(256, 1024, True)))
+    specs.append(("decode_direct_b256", "decode", decode_bytes(256, D), decode(256, 256, False)))
+    specs.append(("decode_direct_b64", "decode", decode_bytes(64, D), decode(64, 64, False)))
+
+    def ring(Bq):
+        def setup():
+            x = torch.randn(Bq, D, device=dev, generator=g).to(BF)
+            rs = torch.randn(Bq, 3, D, device=dev, generator=g).to(BF)
+            seen = torch.randint(1, 8193, (Bq,), device=dev, generator=g, dtype=torch.int32)
+
+            def check():
+                r = rs.clone()
+                y = R.causal_conv1d_update_ring(x, r, w4, b4, "silu", seen)
+                r_out, r_ring = T.ref_update_ring(x, rs, w4, b4, True, seen)
+                return T.within(y, r_out, TOL) and torch.equal(r, r_ring)
+
+            return lambda: R.causal_conv1d_update_ring(x, rs, w4, b4, "silu", seen), check
+
+        return setup
+
+    ring_bytes = lambda Bq: 2 * Bq * D * E + 4 * Bq * D * E + D * 4 * E + D * E + Bq * 4  # noqa: E731
+    specs.append(("decode_ring_b256", "decode", ring_bytes(256), ring(256)))
+    specs.append(("decode_ring_b64", "decode", ring_bytes(64), ring(64)))
+
+    def conv(to):
+        def setup():
+            st = torch.randn(256, D, 3, device=dev, generator=g).to(BF)
+            rg = torch.randn(256, 3, D, device=dev, generator=g).to(BF)
+            seen = torch.randint(1, 8193, (256,), device=dev, generator=g, dtype=torch.int32)
+            if to:
+                return (lambda: R.to_ring(st, seen),
+                        lambda: torch.equal(R.to_ring(st, seen), T.ref_to_ring(st, seen)))
+            return (lambda: R.from_ring(rg, seen),
+                    lambda: torch.equal(R.from_ring(rg, seen), T.ref_from_ring(rg, seen)))
+
+        return setup
+
+    specs.append(("to_ring_b256", "decode", 2 * 256 * D * 3 * E + 256 * 4, conv(True)))
+    specs.append(("from_ring_b256", "decode", 2 * 256 * D * 3 * E + 256 * 4, conv(False)))
+
+    def spec():
+        Bs, S = 64, 4
+        xs = torch.randn(Bs, S, D, device=dev, generator=g).to(BF).transpose(1, 2)
+        st = torch.randn(Bs, D, 3, device=dev, generator=g).to(BF)
+        inter = torch.empty(Bs, S, D, 3, device=dev, dtype=BF)
+        perm = torch.randperm(Bs, device=dev, generator=g).to(torch.int32)
+
+        def check():
+            s2, i2 = st.clone(), torch.zeros_like(inter)
+            y = R.causal_conv1d_update(xs, s2, w4, b4, "silu", perm, -1, i2, perm)
+            r_out, r_st, r_it = T.ref_update(xs, st, w4, b4, True, perm, -1, torch.zeros_like(inter),
+                                             perm)
+            return T.within(y, r_out, TOL) and torch.equal(s2, r_st) and torch.equal(i2, r_it)
+
+        return lambda: R.causal_conv1d_update(xs, st, w4, b4, "silu", perm, -1, inter, perm), check
+
+    specs.append(("spec_decode_b64_s4", "decode",
+                  decode_bytes(64, D, steps=4, idx=True, inter=True), spec))
+
+    # Fused Gated DeltaNet decode at the reference's sglang shape (benchmarks/bench_sglang.py:42,
+    # 202-215): conv over the leading 10240 columns of 16384-wide [Q|K|V|Z] rows, 48 heads,
+    # 310 slots, no bias.
+    def unpack(Bq):
+        Du, cols, heads, slots = 10240, 16384, 48, 310
+
+        def setup():
+            from causal_conv1d_cute import unpack as U
+
+            wu = (torch.randn(Du, 4, device=dev, generator=g) * 0.3).to(BF)
+            st = torch.randn(slots, Du, 3, device=dev, generator=g).to(BF)
+            idx = (torch.randperm(slots - 1, device=dev, generator=g)[:Bq] + 1).to(torch.int32)
+            qkvz = torch.randn(Bq, cols, device=dev, generator=g).to(BF)
+            ba = torch.randn(Bq, 2 * heads, device=dev, generator=g).to(BF)
+            cfg = U.unpack_config(Du, Bq, qkvz.stride(0))
+
+            def check():
+                s2 = st.clone()
+                o, z, b, a = U.causal_conv1d_update_unpack(qkvz, ba, s2, wu, None, idx, heads, "silu",
+                                                           -1, *cfg)
+                r = T.ref_update_unpack(qkvz, ba, st, wu, None, idx, heads, True)
+                return (T.within(o, r[0], TOL) and torch.equal(z, r[1]) and torch.equal(b, r[2])
+                        and torch.equal(a, r[3]) and torch.equal(s2, r[4]))
+
+            return (lambda: U.causal_conv1d_update_unpack(qkvz, ba, st, wu, None, idx, heads, "silu",
+                                                          -1, *cfg), check)
+
+        nbytes = 2 * Bq * Du * E + 2 * Bq * Du * 3 * E + Du * 4 * E + Bq * 4 + 2 * Bq * (cols - Du) * E \
+            + 4 * Bq * heads * E
+        return nbytes, setup
+
+    for Bq in (64, 256):
+        nb, su = unpack(Bq)
+        specs.append((f"unpack_b{Bq}", "decode", nb, su))
+
+    Tv, qsl, cidx, hinit, xv = varlen_batch(dev, g)
+    for Wv in (2, 3, 4, 8):
+        for layout in ("token_major", "channel_first"):
+            def setup(Wv=Wv, layout=layout):
+                wv = _w(g, D, Wv, dev)
+                states = torch.randn(512, D, Wv - 1, device=dev, generator=g).to(BF)
+                x = xv.t() if layout == "token_major" else xv.t().contiguous()
+
+                def check():
+                    s2 = states.clone()
+                    y = R.causal_conv1d_varlen_fn(x, wv, None, qsl, cidx, hinit, s2, "silu")
+                    r_out, r_st = T.ref_varlen(x, wv, None, qsl, cidx, hinit, states, True)
+                    return T.within(y, r_out, TOL) and torch.equal(s2, r_st)
+
+                return lambda: R.causal_conv1d_varlen_fn(x, wv, None, qsl, cidx, hinit, states, "silu"), check
+
+            name = f"varlen_w{Wv}" + ("" if layout == "token_major" else "_channel_first")
+            specs.append((name, "big", varlen_bytes(D, Tv, Wv, hinit), setup))
+    return specs
+
+
+def run_paths(R, T, dev, ours):
+    """Parity-check, then time, every path; returns {name: result}."""
+    flush = Flusher(dev)
+    res = {}
+    for name, kind, nbytes, setup in path_specs(R, T, dev, ours):
+        t0 = time.time()
+        try:
+            call, check = setup()
+            ok = bool(check())
+            r = {"parity": "ok" if ok else "WRONG", "bytes": nbytes}
+            if ok:
+                if kind == "decode":
+                    cold, warm = cold_warm_us(call, flush)
+                    r.update(us_cold=cold, us_warm=warm, gbs_cold=nbytes / (cold * 1e3))
+                else:
+                    us = big_us(call)
+                    r.update(us=us, gbs=nbytes / (us * 1e3))
+        except Exception as e:  # noqa: BLE001
+            r = {"error": f"{type(e).__name__}: {e}"[:500]}
+        r["wall_s"] = round(time.time() - t0, 1)
+        res[name] = r
+        torch.cuda.synchronize()
+    return res
+
+
+def copy_ceiling(dev, headline_us):
+    """The library's own 32-byte-vector copy of the headline's bytes (512 MiB in, 512 MiB out),
+    and torch's copy_ (cudaMemcpyAsync device to device) beside it."""
+    import causal_conv1d_cute.testing as T
+
+    src = torch.randn(B * L * D, device=dev).to(BF)
+    dst = torch.empty_like(src)
+    T.copy_ceiling(dst, src)
+    torch.cuda.synchronize()
+    ok = torch.equal(dst, src)
+    nbytes = 2 * src.numel() * E
+    us = big_us(lambda: T.copy_ceiling(dst, src))
+    us_torch = big_us(lambda: dst.copy_(src))
+    return {"parity": "ok" if ok else "WRONG", "bytes": nbytes, "us": us, "gbs": nbytes / (us * 1e3),
+            "us_torch_copy": us_torch, "headline_over_copy": headline_us / us}
+
+
+# ---------------------------------------------------------------------------------------------
+# The reference's CuTe kernels on the same GPU (child process: the reference's package has the
+# same module name as this library's)
+# ---------------------------------------------------------------------------------------------
+
+
+def _load_testing():
+    """causal_conv1d_cute/testing.py of this library as a standalone module (it needs only
+    torch), for the reference child, where `causal_conv1d_cute` names the reference package."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("cc1d_testing",
+                                                  PKG / "causal_conv1d_cute" / "testing.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def reference_cute_child():
+    import cutlass
+    import cutlass.cute as cute
+
+    tanh = cute.math.tanh
+
+    def tanh_compat(a, fastmath=False, *, approx=None, **kw):
+        return tanh(a, fastmath or bool(approx), **kw)
+
+    cute.math.tanh = tanh_compat
+    import causal_conv1d_cute as R
+    from causal_conv1d_cute import fallback
+
+    assert Path(R.__file__).resolve().is_relative_to(REF_PKG.resolve()), R.__file__
+
+    def refuse(why):
+        raise RuntimeError(f"the reference would fall back to PyTorch: {why}")
+
+    fallback.warn = refuse
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    T = _load_testing()
+    res = {"impl": "reference CuTe DSL kernels (baseline/_ref, unmodified)",
+           "cutlass_dsl": getattr(cutlass, "__version__", None),
+           "compat": "cute.math.tanh(approx=True) forwarded to fastmath=True (DSL 4.5.0 spelling)"}
+    x = torch.randn(B, L, D, device=dev).to(BF).transpose(1, 2)
+    w4 = (torch.rand(D, 4, device=dev) - 0.5).to(BF)
+    b4 = (torch.randn(D, device=dev) * 0.1).to(BF)
+    out = torch.empty(B, L, D, device=dev, dtype=BF).transpose(1, 2)
+    ok = _rows_within(R.causal_conv1d_fn(x, w4, b4, "silu"), x, w4, b4, T)
+    us = big_us(lambda: R.causal_conv1d_fn(x, w4, b4, "silu", out=out))
+    res["prefill_config2"] = {"parity": "ok" if ok else "WRONG", "us": us,
+                              "gbs": HEADLINE_BYTES / (us * 1e3), "bytes": HEADLINE_BYTES}
+    del x, out
+    res["paths"] = run_paths(R, T, dev, ours=False)
+    print("REFERENCE_CUTE " + json.dumps(res), flush=True)
+
+
+def reference_cute(timeout=1200):
+    if not (REF_PKG / "causal_conv1d_cute").exists():
+        return {"unavailable": "the reference package is not installed under baseline/_ref"}
+    t0 = time.time()
+    try:
+        r = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--reference-cute-child"],
+                           capture_output=True, text=True, timeout=timeout, cwd=str(ROOT))
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"the reference CuTe run did not finish in {timeout} s"}
+    for line in r.stdout.splitlines():
+        if line.startswith("REFERENCE_CUTE "):
+            d = json.loads(line[len("REFERENCE_CUTE "):])
+            d["wall_s"] = round(time.time() - t0, 1)
+            return d
+    return {"unavailable": f"the reference CuTe run failed (rc {r.returncode}): "
+                           + (r.stderr or r.stdout)[-800:]}
+
+
+# ---------------------------------------------------------------------------------------------
+# Headline: prefill config 2, channel-sliced over the ranks
+# ---------------------------------------------------------------------------------------------
 
 
 def run_headline(args, rank, world, device):
     import causal_conv1d_cute as C
+    from causal_conv1d_cute import testing as T
 
-    x, w, bias = make_prefill(device, 1234 + rank)
-    xv = x.transpose(1, 2)  # (B, D, L) channel-last view
-    out = torch.empty(B, L, D, device=device, dtype=torch.bfloat16).transpose(1, 2)
+    Dr = D // world
+    lo = rank * Dr
+    # Every rank draws the whole layer from the same seed and keeps its own channel slice as a
+    # contiguous activation, as a tensor-parallel rank holds its shard.
+    g = torch.Generator(device=device).manual_seed(1234)
+    xg = torch.randn(B, L, D, device=device, generator=g).to(BF)
+    wg = _w(g, D, W, device)
+    bg = _b(g, D, device)
+    x = xg[:, :, lo:lo + Dr].contiguous()
+    w, bias = wg[lo:lo + Dr].contiguous(), bg[lo:lo + Dr].contiguous()
+    del xg
+    xv = x.transpose(1, 2)  # (B, Dr, L) channel-last view
+    out = torch.empty(B, L, Dr, device=device, dtype=BF).transpose(1, 2)
+    rank_bytes = 2 * B * L * Dr * E + Dr * W * E + Dr * E
 
     def step():
         C.causal_conv1d_fn(xv, w, bias, "silu", out=out)
 
+    step()
+    torch.cuda.synchronize()
+    parity = _rows_within(out, xv, w, bias, T)
     for _ in range(args.warmup):
         step()
     dist_barrier(world)
@@ -238,17 +689,16 @@ def run_headline(args, rank, world, device):
     # End to end through the public API: pinned host input in, result back to pinned host memory.
     # Every batch row is cut into E2E_CHUNKS token chunks, pipelined over three streams: chunk
     # i + 1 uploads while chunk i is convolved and chunk i - 1 downloads (PCIe carries both
-    # directions at once; more, smaller chunks shorten the pipeline's fill and drain). Chunk k > 0
-    # of a row is convolved over the window that starts W - 1 tokens earlier (already on the
-    # device), into its own output buffer whose first W - 1 rows are discarded, so every output is
-    # computed from its full history. Every step moves the whole input in and the whole result
-    # out; the step ends when the last chunk is back on the host.
+    # directions at once). Chunk k > 0 of a row is convolved over the window that starts W - 1
+    # tokens earlier (already on the device), into its own output buffer whose first W - 1 rows
+    # are discarded, so every output is computed from its full history. Every step moves the
+    # whole input in and the whole result out; the step ends when the last chunk is on the host.
     Lc = L // E2E_CHUNKS
-    xh = torch.empty(B, L, D, dtype=torch.bfloat16, pin_memory=True)
+    xh = torch.empty(B, L, Dr, dtype=BF, pin_memory=True)
     xh.copy_(x)
-    oh = torch.empty(B, L, D, dtype=torch.bfloat16, pin_memory=True)
+    oh = torch.empty(B, L, Dr, dtype=BF, pin_memory=True)
     xd = torch.empty_like(x)
-    yc = torch.empty(B, E2E_CHUNKS, Lc + W - 1, D, device=device, dtype=torch.bfloat16)
+    yc = torch.empty(B, E2E_CHUNKS, Lc + W - 1, Dr, device=device, dtype=BF)
     s_in, s_cmp, s_out = (torch.cuda.Stream(device) for _ in range(3))
 
     def e2e_step():
@@ -266,9 +716,9 @@ def run_headline(args, rank, world, device):
                     up.record(s_in)
                 s_cmp.wait_event(up)
                 with torch.cuda.stream(s_cmp):
-                    lo = max(t0 - (W - 1), 0)
-                    dst = yc[i, k, W - 1 - (t0 - lo):]
-                    C.causal_conv1d_fn(xd[i : i + 1, lo:t1].transpose(1, 2), w, bias, "silu",
+                    lo_ = max(t0 - (W - 1), 0)
+                    dst = yc[i, k, W - 1 - (t0 - lo_):]
+                    C.causal_conv1d_fn(xd[i:i + 1, lo_:t1].transpose(1, 2), w, bias, "silu",
                                        out=dst.unsqueeze(0).transpose(1, 2))
                     done = torch.cuda.Event()
                     done.record(s_cmp)
@@ -286,21 +736,23 @@ def run_headline(args, rank, world, device):
     e2e_ms = allreduce_max(e2e_ms, world, device)
     torch.cuda.synchronize()
     # The result read back must equal the device result.
-    assert torch.equal(oh.to(device), out.transpose(1, 2))
+    parity = parity and torch.equal(oh.to(device), out.transpose(1, 2))
+    parity = allreduce_min_flag(parity, world, device)
 
-    value = HEADLINE_BYTES * world * args.steps / (total_ms / 1e3) / 1e9
-    e2e_value = HEADLINE_BYTES * world * e2e_steps / (e2e_ms / 1e3) / 1e9
-    achieved = HEADLINE_BYTES / (avg_launch_ms / 1e3) / 1e9
+    value = HEADLINE_BYTES * args.steps / (total_ms / 1e3) / 1e9
+    e2e_value = HEADLINE_BYTES * e2e_steps / (e2e_ms / 1e3) / 1e9
+    achieved = rank_bytes / (avg_launch_ms / 1e3) / 1e9
     peak, peak_kind = peaks()
-    traffic = profiled_traffic(HEADLINE_KERNEL)
+    traffic = profiled_traffic(HEADLINE_KERNEL) if world == 1 else None
     return {
         "value": value,
         "ms_per_step": total_ms / args.steps,
+        "parity": "ok" if parity else "WRONG",
         "e2e": {
             "value": e2e_value,
             "unit": "GB/s",
-            "h2d_bytes_per_step": xh.numel() * xh.element_size(),
-            "d2h_bytes_per_step": oh.numel() * oh.element_size(),
+            "h2d_bytes_per_step": xh.numel() * xh.element_size() * world,
+            "d2h_bytes_per_step": oh.numel() * oh.element_size() * world,
             "ms_per_step": e2e_ms / e2e_steps,
         },
         "roofline": {
@@ -312,180 +764,110 @@ def run_headline(args, rank, world, device):
             "traffic": traffic,
             "peak_source": f"{peak_kind} hbm_gbs (copy, burst)",
             "kernel": HEADLINE_KERNEL,
-            "algorithmic_bytes_per_launch": HEADLINE_BYTES,
+            "algorithmic_bytes_per_launch": rank_bytes,
             "avg_launch_us": avg_launch_ms * 1e3,
+            "frac_of_8tbs_nominal": achieved / 8000.0,
         },
         "clocks": sampler.summary(),
         "gpu_launches": args.steps,
+        "avg_launch_us": avg_launch_ms * 1e3,
     }
 
 
 # ---------------------------------------------------------------------------------------------
-# Other BASELINE paths (N = 1)
+# Distributed plumbing and the sharded checks
 # ---------------------------------------------------------------------------------------------
 
 
-def _median_us(per_ms):
-    return statistics.median(per_ms) * 1e3
+def dist_barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
 
 
-def graph_us(calls, reps):
-    """Microseconds per call of `calls` (one callable per input set) replayed in a CUDA graph.
-
-    All calls are captured once, back to back, and the graph is replayed `reps` times between two
-    events, so host launch overhead is excluded and every call follows the previous one as it
-    would inside a captured serving step.
-    """
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        for f in calls:
-            f()
-    torch.cuda.current_stream().wait_stream(side)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        for f in calls:
-            f()
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(reps):
-        graph.replay()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b) * 1e3 / (reps * len(calls))
+def allreduce_max(v, world, device):
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
 
 
-def run_paths(device, reps=50, sets=8):
-    """Decode paths: `sets` independent input sets (together larger than L2) are cycled, so each
-    call reads cold data ("cold"); "warm" repeats one set. Varlen inputs exceed L2 by themselves."""
+def allreduce_min_flag(ok, world, device):
+    if world == 1:
+        return bool(ok)
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def sharded_paths(rank, world, device):
+    """Config 2, config 3 and config 5 (W = 4) with D/N channels per rank: every rank's whole
+    output (and state cache) all-gathered and compared bit for bit with the unsharded run on rank
+    0; config 3 and config 5 also timed per rank (max over ranks)."""
     import causal_conv1d_cute as C
+    from causal_conv1d_cute import shard
 
-    g = torch.Generator(device=device).manual_seed(7)
-    bf = torch.bfloat16
     res = {}
-    w4 = (torch.rand(D, 4, device=device, generator=g) - 0.5).to(bf)
-    bias = (torch.randn(D, device=device, generator=g) * 0.1).to(bf)
+    g = torch.Generator(device=device).manual_seed(99)
 
-    def record(name, calls, nbytes, extra=None):
-        cold = graph_us(calls, reps)
-        warm = graph_us(calls[:1] * len(calls), reps)
-        res[name] = {"us_cold": cold, "us_warm": warm, "bytes": nbytes,
-                     "gbs_cold": nbytes / (cold * 1e3), **(extra or {})}
+    # Config 2: the rank's channel slice made contiguous (its own activation), as timed above.
+    x = torch.randn(B, L, D, device=device, generator=g).to(BF).transpose(1, 2)
+    w4, b4 = _w(g, D, 4, device), _b(g, D, device)
 
-    # Config 2 stored channel-first: contiguous (8, 8192, 4096) (the reference's "bdl" layout).
-    xcf = torch.randn(B, D, L, device=device, generator=g).to(bf)
-    ocf = torch.empty_like(xcf)
-    us = graph_us([lambda: C.causal_conv1d_fn(xcf, w4, bias, "silu", out=ocf)], 20)
-    res["prefill_channel_first"] = {"us": us, "bytes": HEADLINE_BYTES, "gbs": HEADLINE_BYTES / (us * 1e3)}
-    del xcf, ocf
+    def prefill(xs, ws, bs):
+        xc = xs.transpose(1, 2).contiguous().transpose(1, 2)
+        return C.causal_conv1d_fn(xc, ws.contiguous(), bs.contiguous(), "silu")
 
-    # Config 2 with the Dao-interface extras: initial states in, final states out (channel-last
-    # states, as upstream allocates them). Algorithmic bytes add 2 * B * D * 3 elements.
-    xs = torch.randn(B, L, D, device=device, generator=g).to(bf).transpose(1, 2)
-    init = torch.randn(B, 3, D, device=device, generator=g).to(bf).transpose(1, 2)
-    fin = torch.empty_like(init)
-    nbytes = HEADLINE_BYTES + 2 * B * D * 3 * 2
-    us = graph_us([lambda: C.causal_conv1d_fwd_states(xs, w4, bias, None, init, True, fin, "silu")], 20)
-    res["prefill_states"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3)}
-    seq = torch.zeros(B, L, device=device, dtype=torch.int32)
-    seq[:, L // 2:] = 1
-    us = graph_us([lambda: C.causal_conv1d_fwd_states(xs, w4, bias, seq, None, False, None, "silu")], 20)
-    nbytes = HEADLINE_BYTES + B * L * 4
-    res["prefill_seq_idx"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3)}
-    del xs, init, fin, seq
+    ok = shard.sharded_equals_unsharded(prefill, [x, w4, b4], [1, 0, 0], 1, rank, world, device)
+    res["prefill_config2"] = "bit-identical" if ok else "MISMATCH"
+    del x
 
-    # Config 3: single-token indexed decode, B=256, 1024-slot cache (48 MiB per set).
-    Bd, slots = 256, 1024
-    calls = []
-    for _ in range(sets):
-        x = torch.randn(Bd, D, device=device, generator=g).to(bf)
-        cache = torch.randn(slots, D, 3, device=device, generator=g).to(bf)
-        idx = torch.randperm(slots, device=device, generator=g)[:Bd].to(torch.int32)
-        calls.append(lambda x=x, cache=cache, idx=idx: C.causal_conv1d_update(x, cache, w4, bias, "silu", idx))
-    nbytes = 2 * Bd * D * 2 + 2 * Bd * D * 3 * 2 + D * 4 * 2 + D * 2 + Bd * 4
-    record("decode_indexed_b256", calls, nbytes)
+    # Config 3: indexed decode, B = 256, 1024-slot cache.
+    xd = torch.randn(256, D, device=device, generator=g).to(BF)
+    cache = torch.randn(1024, D, 3, device=device, generator=g).to(BF)
+    idx = torch.randperm(1024, device=device, generator=g)[:256].to(torch.int32)
 
-    # The reference's published decode shapes (B300): direct (non-indexed) state at B = 256 and
-    # B = 64, and ring decode at B = 64, for a like-for-like comparison.
-    for Bq in (256, 64):
-        calls = []
-        for _ in range(sets):
-            x = torch.randn(Bq, D, device=device, generator=g).to(bf)
-            st = torch.randn(Bq, D, 3, device=device, generator=g).to(bf)
-            calls.append(lambda x=x, st=st: C.causal_conv1d_update(x, st, w4, bias, "silu"))
-        nbytes = 2 * Bq * D * 2 + 2 * Bq * D * 3 * 2 + D * 4 * 2 + D * 2
-        record(f"decode_direct_b{Bq}", calls, nbytes)
-    calls = []
-    for _ in range(sets):
-        x = torch.randn(64, D, device=device, generator=g).to(bf)
-        ring = torch.randn(64, 3, D, device=device, generator=g).to(bf)
-        seen = torch.randint(1, 8193, (64,), device=device, generator=g, dtype=torch.int32)
-        calls.append(lambda x=x, ring=ring, seen=seen: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen))
-    record("decode_ring_b64", calls, 2 * 64 * D * 2 + 4 * 64 * D * 2 + D * 4 * 2 + D * 2 + 64 * 4)
+    def decode(xs, cs, ws, bs, ix):
+        c = cs.contiguous().clone()
+        y = C.causal_conv1d_update(xs.contiguous(), c, ws.contiguous(), bs.contiguous(), "silu", ix)
+        return y, c
 
-    # Config 3 ring variant: ring (256, 3, 8192), seen ~U[1, 8192].
-    calls = []
-    for _ in range(sets):
-        x = torch.randn(Bd, D, device=device, generator=g).to(bf)
-        ring = torch.randn(Bd, 3, D, device=device, generator=g).to(bf)
-        seen = torch.randint(1, 8193, (Bd,), device=device, generator=g, dtype=torch.int32)
-        calls.append(lambda x=x, ring=ring, seen=seen: C.causal_conv1d_update_ring(x, ring, w4, bias, "silu", seen))
-    nbytes = 2 * Bd * D * 2 + 3 * Bd * D * 2 + Bd * D * 2 + D * 4 * 2 + D * 2 + Bd * 4
-    record("decode_ring_b256", calls, nbytes)
+    ok = shard.sharded_equals_unsharded(decode, [xd, cache, w4, b4, idx], [1, 1, 0, 0, None],
+                                        (1, 1), rank, world, device)
+    lo, hi = shard.channel_slice(D, rank, world)
+    xr, cr = xd[:, lo:hi].contiguous(), cache[:, lo:hi].contiguous()
+    wr, br = w4[lo:hi].contiguous(), b4[lo:hi].contiguous()
+    flush = Flusher(device)
+    dist_barrier(world)
+    cold, warm = cold_warm_us(lambda: C.causal_conv1d_update(xr, cr, wr, br, "silu", idx), flush)
+    cold, warm = allreduce_max(cold, world, device), allreduce_max(warm, world, device)
+    nb = decode_bytes(256, D, idx=True)
+    res["decode_indexed_b256"] = {"check": "bit-identical" if ok else "MISMATCH", "us_cold": cold,
+                                  "us_warm": warm, "gbs_cold": nb / (cold * 1e3), "bytes": nb,
+                                  "dim_per_gpu": hi - lo}
+    del cache, cr
 
-    # Ring layout conversions at the config-3 ring shape (the state a prefill hands to ring
-    # decode, and back): read and write 256 x 8192 x 3 elements each.
-    to_calls, from_calls = [], []
-    for _ in range(sets):
-        st = torch.randn(Bd, D, 3, device=device, generator=g).to(bf)
-        ring = torch.randn(Bd, 3, D, device=device, generator=g).to(bf)
-        seen = torch.randint(1, 8193, (Bd,), device=device, generator=g, dtype=torch.int32)
-        to_calls.append(lambda st=st, seen=seen: C.to_ring(st, seen))
-        from_calls.append(lambda ring=ring, seen=seen: C.from_ring(ring, seen))
-    nbytes = 2 * Bd * D * 3 * 2 + Bd * 4
-    record("to_ring_b256", to_calls, nbytes)
-    record("from_ring_b256", from_calls, nbytes)
+    # Config 5 at W = 4, token-major.
+    Tv, qsl, cidx, hinit, xv = varlen_batch(device, g)
+    w4v = _w(g, D, 4, device)
+    states = torch.randn(512, D, 3, device=device, generator=g).to(BF)
 
-    # Config 4: spec-decode verify, B=64, 4 steps, dense per-step states.
-    Bs, S = 64, 4
-    calls = []
-    for _ in range(sets):
-        xs = torch.randn(Bs, S, D, device=device, generator=g).to(bf).transpose(1, 2)
-        st = torch.randn(Bs, D, 3, device=device, generator=g).to(bf)
-        inter = torch.empty(Bs, S, D, 3, device=device, dtype=bf)
-        perm = torch.randperm(Bs, device=device, generator=g).to(torch.int32)
-        calls.append(lambda xs=xs, st=st, inter=inter, perm=perm:
-                     C.causal_conv1d_update(xs, st, w4, bias, "silu", perm, -1, inter, perm))
-    nbytes = 2 * Bs * S * D * 2 + 2 * Bs * D * 3 * 2 + Bs * S * D * 3 * 2 + D * 4 * 2 + D * 2 + 2 * Bs * 4
-    record("spec_decode_b64_s4", calls, nbytes)
+    def varlen(xs, ws, ss, q, ci, hi_):
+        s = ss.contiguous().clone()
+        xc = xs.t().contiguous().t()  # token-major rows of the rank's own channels
+        y = C.causal_conv1d_varlen_fn(xc, ws.contiguous(), None, q, ci, hi_, s, "silu")
+        return y, s
 
-    # Config 5: varlen, 32 lognormal(7, 1) lengths clipped to [1, 8192], token-major x, and the
-    # same batch stored channel-first.
-    rng = np.random.default_rng(0)
-    lens = np.clip(np.round(rng.lognormal(7, 1, 32)), 1, 8192).astype(np.int64)
-    T = int(lens.sum())
-    qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=device, dtype=torch.int32)
-    cidx = torch.from_numpy(rng.choice(512, 32, replace=False).astype(np.int32)).to(device)
-    hinit = torch.from_numpy(rng.random(32) < 0.5).to(device)
-    xv = torch.randn(T, D, device=device, generator=g).to(bf)
-    xc = xv.t().contiguous()
-    for Wv in (2, 3, 4, 8):
-        wv = (torch.rand(D, Wv, device=device, generator=g) - 0.5).to(bf)
-        states = torch.randn(512, D, Wv - 1, device=device, generator=g).to(bf)
-        nh = int(hinit.sum())
-        nbytes = 2 * D * T * 2 + D * (Wv - 1) * 2 * (32 + nh) + 4 * 33 + 4 * 32 + 32 + D * Wv * 2
-        f = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xv.t(), wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
-        us = graph_us([f], 20)
-        res[f"varlen_w{Wv}"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3), "tokens": T}
-        # The same batch stored channel-first: contiguous (8192, T).
-        fc = lambda wv=wv, states=states: C.causal_conv1d_varlen_fn(xc, wv, None, qsl, cidx, hinit, states, "silu")  # noqa: E731
-        us = graph_us([fc], 20)
-        res[f"varlen_w{Wv}_channel_first"] = {"us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e3),
-                                             "tokens": T}
-    del xc
+    ok = shard.sharded_equals_unsharded(varlen, [xv.t(), w4v, states, qsl, cidx, hinit],
+                                        [0, 0, 1, None, None, None], (0, 1), rank, world, device)
+    xr = xv[:, lo:hi].contiguous().t()
+    wr, sr = w4v[lo:hi].contiguous(), states[:, lo:hi].contiguous()
+    dist_barrier(world)
+    us = big_us(lambda: C.causal_conv1d_varlen_fn(xr, wr, None, qsl, cidx, hinit, sr, "silu"))
+    us = allreduce_max(us, world, device)
+    nb = varlen_bytes(D, Tv, 4, hinit)
+    res["varlen_w4"] = {"check": "bit-identical" if ok else "MISMATCH", "us": us,
+                        "gbs": nb / (us * 1e3), "bytes": nb, "tokens": Tv, "dim_per_gpu": hi - lo}
     return res
 
 
@@ -523,101 +905,156 @@ def cpu_baseline(min_seconds=10.0):
 
 
 # ---------------------------------------------------------------------------------------------
-# Distributed plumbing
+# ncu cases: a few launches of one kernel each, with an L2 flush before every launch
 # ---------------------------------------------------------------------------------------------
 
 
-def dist_barrier(world):
-    if world > 1:
-        torch.distributed.barrier()
-
-
-def allreduce_max(v, world, device):
-    if world == 1:
-        return v
-    t = torch.tensor([v], dtype=torch.float64, device=device)
-    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-    return float(t.item())
-
-
-def sharded_check(rank, world, device):
-    """All-gather a sample of every rank's channel slice and compare with the unsharded run."""
+def _profile_fwd(dev, g, width, layout="cl", batch=2):
     import causal_conv1d_cute as C
 
-    Ls, Dg = 128, D * world
-    g = torch.Generator(device=device).manual_seed(99)
-    xg = torch.randn(1, Ls, Dg, device=device, generator=g).to(torch.bfloat16)
-    wg = (torch.rand(Dg, W, device=device, generator=g) - 0.5).to(torch.bfloat16)
-    bg = (torch.randn(Dg, device=device, generator=g) * 0.1).to(torch.bfloat16)
-    lo, hi = rank * D, (rank + 1) * D
-    mine = C.causal_conv1d_fn(xg[:, :, lo:hi].transpose(1, 2), wg[lo:hi], bg[lo:hi], "silu")
-    mine = mine.transpose(1, 2).contiguous()
-    parts = [torch.empty_like(mine) for _ in range(world)]
-    torch.distributed.all_gather(parts, mine)
-    ok = True
-    if rank == 0:
-        full = C.causal_conv1d_fn(xg.transpose(1, 2), wg, bg, "silu").transpose(1, 2)
-        ok = torch.equal(torch.cat(parts, dim=2), full)
-    flag = torch.tensor([1 if ok else 0], device=device)
-    torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MIN)
-    return bool(flag.item())
+    w, b = _w(g, D, width, dev), _b(g, D, dev)
+    if layout == "cl":
+        x = torch.randn(batch, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
+        out = torch.empty(batch, L, D, device=dev, dtype=BF).transpose(1, 2)
+    else:
+        x = torch.randn(batch, D, L, device=dev, generator=g).to(BF)
+        out = torch.empty_like(x)
+    return lambda: C.causal_conv1d_fn(x, w, b, "silu", out=out)
+
+
+def _profile_varlen(dev, g, width, layout, nseq=8):
+    import causal_conv1d_cute as C
+
+    rng = np.random.default_rng(0)
+    lens = np.clip(np.round(rng.lognormal(7, 1, nseq)), 1, 8192).astype(np.int64)
+    T_ = int(lens.sum())
+    qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=dev, dtype=torch.int32)
+    xv = torch.randn(T_, D, device=dev, generator=g).to(BF)
+    x = xv.t() if layout == "token_major" else xv.t().contiguous()
+    w = _w(g, D, width, dev)
+    states = torch.randn(64, D, width - 1, device=dev, generator=g).to(BF)
+    cidx = torch.arange(nseq, device=dev, dtype=torch.int32) * 3
+    hinit = torch.ones(nseq, dtype=torch.bool, device=dev)
+    return lambda: C.causal_conv1d_varlen_fn(x, w, None, qsl, cidx, hinit, states, "silu")
+
+
+def _profile_decode(dev, g, width, case):
+    import causal_conv1d_cute as C
+
+    w, b = _w(g, D, 4, dev), _b(g, D, dev)
+    x = torch.randn(256, D, device=dev, generator=g).to(BF)
+    if case == "decode":
+        cache = torch.randn(1024, D, 3, device=dev, generator=g).to(BF)
+        idx = torch.randperm(1024, device=dev, generator=g)[:256].to(torch.int32)
+        return lambda: C.causal_conv1d_update(x, cache, w, b, "silu", idx)
+    if case == "decode_b64":
+        st = torch.randn(64, D, 3, device=dev, generator=g).to(BF)
+        return lambda: C.causal_conv1d_update(x[:64], st, w, b, "silu")
+    seen = torch.randint(1, 8193, (256,), device=dev, generator=g, dtype=torch.int32)
+    ring = torch.randn(256, 3, D, device=dev, generator=g).to(BF)
+    if case == "ring":
+        return lambda: C.causal_conv1d_update_ring(x, ring, w, b, "silu", seen)
+    st = torch.randn(256, D, 3, device=dev, generator=g).to(BF)
+    if case == "to_ring":
+        return lambda: C.to_ring(st, seen)
+    return lambda: C.from_ring(ring, seen)
+
+
+def _profile_other(dev, g, width, case):
+    import causal_conv1d_cute as C
+
+    w, b = _w(g, D, 4, dev), _b(g, D, dev)
+    if case == "spec":
+        xs = torch.randn(64, 4, D, device=dev, generator=g).to(BF).transpose(1, 2)
+        st = torch.randn(64, D, 3, device=dev, generator=g).to(BF)
+        inter = torch.empty(64, 4, D, 3, device=dev, dtype=BF)
+        perm = torch.randperm(64, device=dev, generator=g).to(torch.int32)
+        return lambda: C.causal_conv1d_update(xs, st, w, b, "silu", perm, -1, inter, perm)
+    if case == "unpack":
+        from causal_conv1d_cute import unpack as U
+
+        wu = (torch.randn(10240, 4, device=dev, generator=g) * 0.3).to(BF)
+        st = torch.randn(310, 10240, 3, device=dev, generator=g).to(BF)
+        idx = (torch.randperm(309, device=dev, generator=g)[:256] + 1).to(torch.int32)
+        qkvz = torch.randn(256, 16384, device=dev, generator=g).to(BF)
+        ba = torch.randn(256, 96, device=dev, generator=g).to(BF)
+        return lambda: U.causal_conv1d_update_unpack(qkvz, ba, st, wu, None, idx, 48, "silu", -1)
+    if case == "states":  # config 2 with batch 2, initial and final states
+        x = torch.randn(2, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
+        init = torch.randn(2, 3, D, device=dev, generator=g).to(BF).transpose(1, 2)
+        fin = torch.empty_like(init)
+        return lambda: C.causal_conv1d_fwd_states(x, w, b, None, init, True, fin, "silu")
+    # copy: the headline's bytes of batch 2 (128 MiB in, 128 MiB out)
+    import causal_conv1d_cute.testing as T
+
+    src = torch.randn(2 * L * D, device=dev).to(BF)
+    dst = torch.empty_like(src)
+    return lambda: T.copy_ceiling(dst, src)
+
+
+PROFILE_CASES = {
+    "fwd": lambda d, g, w: _profile_fwd(d, g, w, "cl"),
+    "fwd_cf": lambda d, g, w: _profile_fwd(d, g, w, "cf"),
+    "varlen": lambda d, g, w: _profile_varlen(d, g, w, "token_major"),
+    "varlen_cf": lambda d, g, w: _profile_varlen(d, g, w, "channel_first"),
+    "decode": lambda d, g, w: _profile_decode(d, g, w, "decode"),
+    "decode_b64": lambda d, g, w: _profile_decode(d, g, w, "decode_b64"),
+    "ring": lambda d, g, w: _profile_decode(d, g, w, "ring"),
+    "to_ring": lambda d, g, w: _profile_decode(d, g, w, "to_ring"),
+    "from_ring": lambda d, g, w: _profile_decode(d, g, w, "from_ring"),
+    "spec": lambda d, g, w: _profile_other(d, g, w, "spec"),
+    "unpack": lambda d, g, w: _profile_other(d, g, w, "unpack"),
+    "states": lambda d, g, w: _profile_other(d, g, w, "states"),
+    "copy": lambda d, g, w: _profile_other(d, g, w, "copy"),
+}
 
 
 def profile_case(case, device, width=W):
-    """A few launches of one kernel, sized for an ncu capture (a few hundred MB on the device)."""
-    import causal_conv1d_cute as C
-
+    """4 launches of one path, sized for an ncu capture (a few hundred MB on the device), each
+    after an L2-sized write so that every captured launch starts cold."""
     g = torch.Generator(device=device).manual_seed(0)
-    bf = torch.bfloat16
-    w = (torch.rand(D, width, device=device, generator=g) - 0.5).to(bf)
-    b = (torch.randn(D, device=device, generator=g) * 0.1).to(bf)
-    if case == "fwd":  # config 2 with batch 2: 128 MiB in, 128 MiB out
-        x = torch.randn(2, L, D, device=device, generator=g).to(bf)
-        out = torch.empty_like(x).transpose(1, 2)
-        calls = [lambda: C.causal_conv1d_fn(x.transpose(1, 2), w, b, "silu", out=out)] * 4
-    elif case == "fwd_cf":  # the same batch stored channel-first (2, 8192, 4096) contiguous
-        x = torch.randn(2, D, L, device=device, generator=g).to(bf)
-        out = torch.empty_like(x)
-        calls = [lambda: C.causal_conv1d_fn(x, w, b, "silu", out=out)] * 4
-    elif case in ("decode", "ring"):  # config 3, full size
-        x = torch.randn(256, D, device=device, generator=g).to(bf)
-        if case == "decode":
-            cache = torch.randn(1024, D, 3, device=device, generator=g).to(bf)
-            idx = torch.randperm(1024, device=device, generator=g)[:256].to(torch.int32)
-            calls = [lambda: C.causal_conv1d_update(x, cache, w, b, "silu", idx)] * 4
-        else:
-            ring = torch.randn(256, 3, D, device=device, generator=g).to(bf)
-            seen = torch.randint(1, 8193, (256,), device=device, generator=g, dtype=torch.int32)
-            calls = [lambda: C.causal_conv1d_update_ring(x, ring, w, b, "silu", seen)] * 4
-    elif case == "spec":  # config 4, full size
-        xs = torch.randn(64, 4, D, device=device, generator=g).to(bf).transpose(1, 2)
-        st = torch.randn(64, D, 3, device=device, generator=g).to(bf)
-        inter = torch.empty(64, 4, D, 3, device=device, dtype=bf)
-        perm = torch.randperm(64, device=device, generator=g).to(torch.int32)
-        calls = [lambda: C.causal_conv1d_update(xs, st, w, b, "silu", perm, -1, inter, perm)] * 4
-    else:  # config 5 with 8 of its 32 lognormal sequences
-        rng = np.random.default_rng(0)
-        lens = np.clip(np.round(rng.lognormal(7, 1, 8)), 1, 8192).astype(np.int64)
-        T = int(lens.sum())
-        qsl = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), device=device, dtype=torch.int32)
-        xv = torch.randn(T, D, device=device, generator=g).to(bf)
-        if case == "varlen_cf":  # channel-first: contiguous (8192, T); the call gets x = xv.t()
-            xv = xv.t().contiguous().t()
-        states = torch.randn(64, D, width - 1, device=device, generator=g).to(bf)
-        cidx = torch.arange(8, device=device, dtype=torch.int32) * 3
-        hinit = torch.ones(8, dtype=torch.bool, device=device)
-        calls = [lambda: C.causal_conv1d_varlen_fn(xv.t(), w, None, qsl, cidx, hinit, states, "silu")] * 4
-    # An L2-sized write between launches so every captured launch starts cold.
-    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=device)
-    for f in calls:
-        flush.fill_(1)
-        f()
+    call = PROFILE_CASES[case](device, g, width)
+    flush = Flusher(device)
+    for _ in range(4):
+        flush()
+        call()
     torch.cuda.synchronize()
-    print(json.dumps({"profile": case, "launches": len(calls)}))
+    print(json.dumps({"profile": case, "width": width, "launches": 4}))
+
+
+# ---------------------------------------------------------------------------------------------
+
+
+def reference_cpu_arm(args, rank, n, config):
+    if rank != 0:
+        return
+    from oracle import native
+
+    steps = max(1, args.steps if args.steps < 50 else 20)
+    per_step = []
+    for i in range(min(args.warmup, 2) + steps):
+        cb = cpu_baseline(min_seconds=0.5)
+        if i >= min(args.warmup, 2):
+            per_step.append(cb["value"])
+    v = statistics.median(per_step)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": n,
+        "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+        "cpu_baseline": {"value": v, "unit": "GB/s", "cores": native.threads(), "kind": "port",
+                         "sample": "each step: batch 1 x 256 tokens x 8192 channels of config 2 "
+                                   "for >= 0.5 s, oracle/cc1d_oracle.c (C port of the reference's "
+                                   "fallback.py) with OpenMP"},
+        "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
 
 
 def main():
     args = parse()
+    if args.reference_cute_child:
+        reference_cute_child()
+        return
     if args.profile:
         profile_case(args.profile, torch.device("cuda", 0), args.width)
         return
@@ -627,36 +1064,16 @@ def main():
     n = max(world, 1)
     config = {
         "workload": "prefill_bf16_channel_last (BASELINE config 2)",
-        "batch": B, "seqlen": L, "dim_per_gpu": D, "dim_global": D * n, "width": W,
+        "batch": B, "seqlen": L, "dim": D, "dim_per_gpu": D // n, "width": W,
         "activation": "silu", "bias": True,
         "layout": "x stored (batch, seqlen, dim), passed as its (batch, dim, seqlen) view",
-        "l2": "inputs (512 MiB per GPU) larger than L2 (126 MB); no flush",
-        "parallelism": f"channel-sliced tp{n}: each rank owns {D} channels, no collective in the path",
+        "l2": "inputs (512 MiB) larger than L2 (126 MB); no flush between headline steps; decode "
+              "paths flush 256 MiB before every cold call",
+        "parallelism": f"channel-sliced tp{n}: each rank owns {D // n} of {D} channels, no "
+                       "collective in the path",
     }
     if args.impl == "reference":
-        if rank != 0:
-            return
-        from oracle import native
-
-        steps = max(1, args.steps if args.steps < 50 else 20)
-        per_step = []
-        for i in range(min(args.warmup, 2) + steps):
-            t0 = time.perf_counter()
-            cb = cpu_baseline(min_seconds=0.5)
-            if i >= min(args.warmup, 2):
-                per_step.append(cb["value"])
-        v = statistics.median(per_step)
-        line = {
-            "impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": n,
-            "steps": steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
-            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": native.threads(), "kind": "port",
-                             "sample": "each step: batch 1 x 256 tokens x 8192 channels of config 2 "
-                                       "for >= 0.5 s, oracle/cc1d_oracle.c (C port of the reference's "
-                                       "fallback.py) with OpenMP"},
-            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }
-        print(json.dumps(line))
+        reference_cpu_arm(args, rank, n, config)
         return
 
     if world > 1:
@@ -677,22 +1094,33 @@ def main():
         "warmup": args.warmup,
         "ms_per_step": head["ms_per_step"],
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
         "config": config,
+        "parity": head["parity"],
         "e2e": head["e2e"],
         "roofline": head["roofline"],
         "clocks": head["clocks"],
         "gpu_launches": head["gpu_launches"],
     }
     if world > 1:
-        line["sharded_check"] = "bit-identical" if sharded_check(rank, world, device) else "MISMATCH"
+        line["sharded"] = sharded_paths(rank, world, device)
     if rank == 0 and n == 1:
+        line["copy_ceiling"] = copy_ceiling(device, head["avg_launch_us"])
         if not args.no_paths:
-            line["paths"] = run_paths(device)
+            import causal_conv1d_cute as C
+            from causal_conv1d_cute import testing as T
+
+            line["paths"] = run_paths(C, T, device, ours=True)
+            bad = [k for k, v in line["paths"].items() if v.get("parity") != "ok"]
+            if bad:
+                line["parity"] = "WRONG"
+                line["parity_failed"] = bad
         line["cpu_baseline"] = cpu_baseline()
+        if not args.no_reference_cute:
+            line["reference_cute"] = reference_cute()
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()

@@ -39,6 +39,7 @@ SIGNATURES = {
                     _p, _p, _p, _i64, _i64, _i64, _i64, _i32, _i64, _i32, _i32, _i32, _p, _p],
     "cc1d_update_unpack": [_p, _i64, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _p, _p, _i32,
                            _i64, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _p],
+    "cc1d_copy": [_p, _p, _i64, _p],
 }
 
 EXPORTS = ("cc1d_abi_version", "cc1d_status_string", "cc1d_last_error", *SIGNATURES)

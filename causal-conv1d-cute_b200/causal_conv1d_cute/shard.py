@@ -44,20 +44,27 @@ def max_over_ranks(value, device, world, group=None):
 
 def sharded_equals_unsharded(run, inputs, axes, out_axis, rank, world, device, group=None):
     """Run `run` on this rank's channel slice of every input, gather the outputs and compare them
-    with `run` on the full inputs (rank 0). Returns the verdict on every rank.
+    with `run` on the full inputs (rank 0), bit for bit. Returns the verdict on every rank.
 
     Args:
-        run: callable(*tensors) -> output tensor.
+        run: callable(*tensors) -> output tensor, or a tuple of output tensors (for instance an
+            output and a state cache the call updated).
         inputs: full (unsharded) tensors, identical on every rank.
         axes: channel axis of each input (None: replicated, passed whole).
-        out_axis: channel axis of the output.
+        out_axis: channel axis of the output, or a tuple with one axis per output.
     """
     mine = run(*[t if a is None else shard(t, a, rank, world) for t, a in zip(inputs, axes)])
-    full = gather_channels(mine, out_axis, world, group)
+    single = not isinstance(mine, (tuple, list))
+    mine = (mine,) if single else tuple(mine)
+    oax = (out_axis,) if single else tuple(out_axis)
+    if len(oax) != len(mine):
+        raise ValueError(f"{len(mine)} outputs but {len(oax)} output axes")
+    full = [gather_channels(m, a, world, group) for m, a in zip(mine, oax)]
     ok = True
     if rank == 0:
         ref = run(*inputs)
-        ok = full.shape == ref.shape and torch.equal(full, ref.contiguous())
+        ref = (ref,) if single else tuple(ref)
+        ok = all(f.shape == r.shape and torch.equal(f, r.contiguous()) for f, r in zip(full, ref))
     flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
     return bool(flag.item())

@@ -205,9 +205,56 @@ def ref_update_ring(x, ring, w, b, silu, seen, idx=None, pad=-1):
     return out, rg
 
 
+def ref_to_ring(state, seen):
+    """Ordered state (slots, dim, K) -> ring (slots, K, dim): ring row (seen + k) % K holds entry
+    k (ring.py:33-49)."""
+    S, D, K = state.shape
+    rows = (seen.long().unsqueeze(1) + torch.arange(K, device=state.device)) % K
+    ring = torch.empty(S, K, D, dtype=state.dtype, device=state.device)
+    ring[torch.arange(S, device=state.device).unsqueeze(1), rows] = state.transpose(1, 2)
+    return ring
+
+
+def ref_from_ring(ring, seen):
+    """Ring (slots, K, dim) -> ordered state (slots, dim, K) (ring.py:52-67)."""
+    S, K, D = ring.shape
+    rows = (seen.long().unsqueeze(1) + torch.arange(K, device=ring.device)) % K
+    return ring[torch.arange(S, device=ring.device).unsqueeze(1), rows].transpose(1, 2).contiguous()
+
+
+def ref_update_unpack(qkvz, ba, state, w, b, idx, heads, silu, pad=-1):
+    """Fused Gated DeltaNet decode (unpack.py:33-222) -> (fp32 conv output, z, b, a, state
+    after): the conv reads the leading dim columns of each row; rows whose slot is the pad id or
+    outside the cache keep their state and output their conv input."""
+    D = w.shape[0]
+    zdim = qkvz.shape[1] - D
+    x = qkvz[:, :D]
+    slots = idx.long()
+    valid = (slots != pad) & (slots >= 0) & (slots < state.shape[0])
+    out, st, _ = ref_update(x[valid], state, w, b, silu, idx[valid])
+    full = x.float().clone()
+    full[valid] = out
+    return (full, qkvz[:, D:D + zdim].clone(), ba[:, :heads].clone(), ba[:, heads:2 * heads].clone(),
+            st)
+
+
 def within(got, ref, tol):
     """|got - ref| <= tol + tol |ref| wherever ref is not NaN (NaN marks undefined outputs)."""
     got, ref = got.float(), ref.float()
     keep = ~torch.isnan(ref)
     err = (got - ref).abs()
     return bool(((err <= tol + tol * ref.abs()) | ~keep).all())
+
+
+def copy_ceiling(dst, src):
+    """Copy src into dst (same number of bytes, CUDA, 32-byte aligned) with the library's own
+    32-byte-vector copy kernel (cc1d_copy) on the current stream: the measured ceiling that the
+    streaming kernels are reported against (reference benchmarks/copy_baseline.py:38-90)."""
+    from ._lib import check, load
+
+    n = src.numel() * src.element_size()
+    if dst.numel() * dst.element_size() != n or not (src.is_contiguous() and dst.is_contiguous()):
+        raise ValueError("copy_ceiling needs contiguous tensors of the same size in bytes")
+    stream = torch.cuda.current_stream(src.device).cuda_stream
+    check(load().cc1d_copy(dst.data_ptr(), src.data_ptr(), n, stream))
+    return dst

@@ -320,4 +320,15 @@ cc1d_status_t cc1d_update_unpack(const void* qkvz, int64_t q_sb, const void* ba,
                      "cc1d_update_unpack");
 }
 
+cc1d_status_t cc1d_copy(void* dst, const void* src, int64_t bytes, void* stream) {
+    if (bytes < 0) return fail(CC1D_ERR_INVALID, "negative size");
+    if (bytes == 0) return ok();
+    if (!dst || !src) return fail(CC1D_ERR_INVALID, "a required pointer is NULL");
+    if (overlap(dst, bytes, src, bytes)) return fail(CC1D_ERR_INVALID, "dst overlaps src");
+    if (!cc1d::host_aligned32(dst) || !cc1d::host_aligned32(src))
+        return fail(CC1D_ERR_LAYOUT, "the copy needs 32-byte aligned pointers");
+    if (cc1d_status_t s = bind_stream(stream)) return s;
+    return from_cuda(cc1d::launch_copy(dst, src, bytes, (cudaStream_t)stream), "cc1d_copy");
+}
+
 }  // extern "C"

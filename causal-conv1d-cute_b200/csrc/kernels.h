@@ -135,5 +135,6 @@ cudaError_t launch_ring(const RingArgs& a, int width, int dtype, cudaStream_t st
 cudaError_t launch_ring_convert(const RingConvArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_varlen(const VarArgs& a, int width, int dtype, cudaStream_t stream);
 cudaError_t launch_unpack(const UnpackArgs& a, int width, int dtype, cudaStream_t stream);
+cudaError_t launch_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream);
 
 }  // namespace cc1d

@@ -206,6 +206,16 @@ cc1d_status_t cc1d_update_unpack(const void* qkvz, int64_t q_sb, const void* ba,
                                  int32_t width, int32_t dtype, int32_t gdtype, int32_t silu,
                                  void* stream);
 
+/*
+ * Device-to-device copy of `bytes` bytes (src and dst on the stream's device, 32-byte aligned,
+ * not overlapping) with 32-byte accesses from one wave of CTAs. It is the
+ * measured ceiling the streaming kernels are reported against: a prefill moves the same bytes
+ * (each input read once, each output written once) and adds only its arithmetic.
+ * Replaces: the reference's copy ceiling, benchmarks/copy_baseline.py:38-90 (a D2D copy of a
+ * prefill's bytes timed beside every prefill kernel, benchmarks/BASELINES.md:44).
+ */
+cc1d_status_t cc1d_copy(void* dst, const void* src, int64_t bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

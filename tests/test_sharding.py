@@ -34,6 +34,13 @@ def _varlen_states(x, w, states, qsl):
     return torch.from_numpy(st)
 
 
+def _varlen_both(x, w, states, qsl):
+    """Oracle varlen returning (output, updated state cache)."""
+    out, st = oracle.varlen(x.numpy(), w.numpy(), None, qsl.numpy(), None,
+                            np.ones(len(qsl) - 1, np.uint8), states.numpy(), False, -1, "f32")
+    return torch.from_numpy(out), torch.from_numpy(st)
+
+
 def _worker(rank, world, port, result):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -50,12 +57,16 @@ def _worker(rank, world, port, result):
         ok2 = shard.sharded_equals_unsharded(
             lambda a, ww, s, q: _varlen_states(a, ww, s, q), [xv, w, st, qsl], [0, 0, 1, None], 1,
             rank, world, "cpu")
+        # Several outputs: the output and the state cache of a packed prefill.
+        ok3 = shard.sharded_equals_unsharded(
+            lambda a, ww, s, q: _varlen_both(a, ww, s, q), [xv, w, st, qsl], [0, 0, 1, None],
+            (0, 1), rank, world, "cpu")
         # A deliberately wrong shard (a planted mistake in the oracle output) must be caught.
         bad = shard.sharded_equals_unsharded(
             lambda a, ww, bb: _prefill(a, ww, bb) + (rank == 1) * (a.shape[1] < D), [x, w, b],
             [1, 0, 0], 1, rank, world, "cpu")
         slowest = shard.max_over_ranks(1.0 + rank, "cpu", world)
-        result[rank] = (ok1, ok2, bad, slowest)
+        result[rank] = (ok1, ok2 and ok3, bad, slowest)
     finally:
         dist.destroy_process_group()
 
