@@ -156,69 +156,94 @@ __global__ void __launch_bounds__(kUpdThreads)
                                               threadIdx.x * (LMAX + K - 1));
 }
 
-// Single-step decode without per-step states, the serving hot case, kept lean: one row per
-// thread, raw tap-major weights widened at use, no runtime step loop (the general kernel's 90
-// registers halve the resident threads). Every load is issued before any compute, the slot load
-// first since it heads the only dependent chain (slot -> state); a row with the pad slot or a
-// slot outside the cache skips the state load and all stores. CHECK (a status word was given)
-// adds the report of slots outside the cache, which costs 0.35 us per call, so the unchecked
-// variant leaves it out. Measured on B200 at B = 256, D = 8192 (CUDA-graph replay, cold L2):
-// 8.25 us per call unchecked; 9.4 us with the state load placed behind the slot checks.
-template <typename T, int W, int SS, bool CHECK>
-__global__ void __launch_bounds__(kUpdThreads, 1) decode1_kernel(const UpdArgs a) {
+// Single-step decode without per-step states, the serving hot case, kept lean: R batch rows per
+// thread (gridDim.y == ceil(B / R)), raw tap-major weights widened at use, no runtime step loop
+// (the general kernel's 90 registers halve the resident threads). Every load is issued before any
+// compute: the slot loads first, since each heads the only dependent chain (slot -> state), then
+// the filter and the x rows, then the state blocks of every row; a row with the pad slot or a slot
+// outside the cache skips its state load and all its stores. CHECK (a status word was given) adds
+// the report of slots outside the cache, which costs 0.35 us per call, so the unchecked variant
+// leaves it out.
+//
+// R = 2 with at least 7 resident CTAs per SM (72 registers) runs a batch of 256 rows in one wave
+// of CTAs, every thread keeping two rows' loads in flight; R = 1 (54 registers, 9 CTAs per SM)
+// needs 1.5 waves there. Measured on B200 at D = 8192, bf16, W = 4 (CUDA graphs, L2 flushed before
+// every call; R = 1 / R = 2, us): indexed B = 256, 1024-slot cache: 7.99 / 7.37 cold, 7.47 / 7.07
+// warm; direct B = 256: 7.78 / 7.27 cold. At B = 64 (one wave either way) R = 1 is faster: 3.48 /
+// 4.00 cold. Forms tried and not kept, all within 0.5 us of these: 16 channels per thread with
+// 32-byte accesses (32- to 256-thread CTAs), 4 or 8 rows per thread, the warp's state block moved
+// through shared memory with 512-byte coalesced accesses. The floor under them: an empty kernel on
+// the same grid costs 1.3-1.8 us, and a kernel that only loads the slot, then one 16-byte state
+// vector per thread, costs 5.7-6.3 us cold at B = 256 (two dependent DRAM round trips).
+template <typename T, int W, int SS, bool CHECK, int R>
+__global__ void __launch_bounds__(kUpdThreads, R == 1 ? 1 : 7) decode1_kernel(const UpdArgs a) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
     const int64_t j = (int64_t)blockIdx.x * kUpdThreads + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
-    // One row per thread (gridDim.y == B): a row loop would let the compiler widen the invariant
-    // weights once and keep them in 40 fp32 registers.
-    const int64_t b = blockIdx.y;
-    const int32_t slot = b < a.B ? (a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b) : a.pad;
+    int32_t slot[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t b = (int64_t)blockIdx.y * R + r;
+        slot[r] = b < a.B ? (a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b) : a.pad;
+    }
     uint4 wt[W], bt;
     load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, a.bias != nullptr,
                           wt, bt);
-    uint4 xr;
-    if (b < a.B) xr = ldg16((const T*)a.x + b * a.x_sb + c0);
-    const bool live = slot != a.pad && slot >= 0 && (int64_t)slot < a.nslots;
-    uint4 sr[SS];
-    if (live) {
-        const T* sp = (const T*)a.state + (int64_t)slot * a.s_slot + c0 * SS;
+    uint4 xr[R];
 #pragma unroll
-        for (int q = 0; q < SS; ++q) sr[q] = ld16(sp + q * V);
+    for (int r = 0; r < R; ++r) {
+        const int64_t b = (int64_t)blockIdx.y * R + r;
+        if (b < a.B) xr[r] = ldg16((const T*)a.x + b * a.x_sb + c0);
     }
-    if (CHECK && !live && slot != a.pad && j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
-    if (!live) return;
+    bool live[R];
+    uint4 sr[R][SS];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        live[r] = slot[r] != a.pad && slot[r] >= 0 && (int64_t)slot[r] < a.nslots;
+        if (live[r]) {
+            const T* sp = (const T*)a.state + (int64_t)slot[r] * a.s_slot + c0 * SS;
+#pragma unroll
+            for (int q = 0; q < SS; ++q) sr[r][q] = ld16(sp + q * V);
+        }
+        if (CHECK && !live[r] && slot[r] != a.pad && j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+    }
     const bool use_silu = a.silu != 0;
-    uint4 win[SS];
-    block_to_time<T, SS>(sr, win);
-    float acc[V];
-    unpack16<T>(bt, acc);
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-        float f[V], wk[V];
-        unpack16<T>(win[SS - K + k], f);
-        unpack16<T>(wt[k], wk);
+    for (int r = 0; r < R; ++r) {
+        if (!live[r]) continue;
+        const int64_t b = (int64_t)blockIdx.y * R + r;
+        uint4 win[SS];
+        block_to_time<T, SS>(sr[r], win);
+        float acc[V];
+        unpack16<T>(bt, acc);
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
+        for (int k = 0; k < K; ++k) {
+            float f[V], wk[V];
+            unpack16<T>(win[SS - K + k], f);
+            unpack16<T>(wt[k], wk);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
+        }
+        {
+            float f[V], wk[V];
+            unpack16<T>(xr[r], f);
+            unpack16<T>(wt[K], wk);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), use_silu);
+        }
+        st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
+#pragma unroll
+        for (int s = 0; s + 1 < SS; ++s) win[s] = win[s + 1];
+        win[SS - 1] = xr[r];
+        uint4 blk[SS];
+        time_to_block<T, SS>(win, blk);
+        T* sp = (T*)a.state + (int64_t)slot[r] * a.s_slot + c0 * SS;
+#pragma unroll
+        for (int q = 0; q < SS; ++q) st16(sp + q * V, blk[q]);
     }
-    {
-        float f[V], wk[V];
-        unpack16<T>(xr, f);
-        unpack16<T>(wt[K], wk);
-#pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), use_silu);
-    }
-    st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
-#pragma unroll
-    for (int s = 0; s + 1 < SS; ++s) win[s] = win[s + 1];
-    win[SS - 1] = xr;
-    uint4 blk[SS];
-    time_to_block<T, SS>(win, blk);
-    T* sp = (T*)a.state + (int64_t)slot * a.s_slot + c0 * SS;
-#pragma unroll
-    for (int q = 0; q < SS; ++q) st16(sp + q * V, blk[q]);
 }
 
 // Any strides, any state length S >= W-1 (the whole row shifts by L), any per-step layout.
@@ -300,6 +325,21 @@ cudaError_t launch_vec_inter(const UpdArgs& a, int imode, bool wvec, bool bvec,
     return launch_vec<T, W, SS, LMAX, kInterNone>(a, wvec, bvec, stream);
 }
 
+// The lean single-step decode, R rows per thread, with or without the status report.
+template <typename T, int W, int K, int P, int R>
+cudaError_t launch_decode1(const UpdArgs& a, cudaStream_t stream) {
+    const int64_t nvec = a.D / Vec<T>::V;
+    dim3 grid((unsigned)ceil_div(nvec, kUpdThreads), (unsigned)ceil_div(a.B, (int64_t)R));
+    if (a.status != nullptr) {
+        if (a.S == K) decode1_kernel<T, W, K, true, R><<<grid, kUpdThreads, 0, stream>>>(a);
+        else decode1_kernel<T, W, P, true, R><<<grid, kUpdThreads, 0, stream>>>(a);
+    } else {
+        if (a.S == K) decode1_kernel<T, W, K, false, R><<<grid, kUpdThreads, 0, stream>>>(a);
+        else decode1_kernel<T, W, P, false, R><<<grid, kUpdThreads, 0, stream>>>(a);
+    }
+    return cudaGetLastError();
+}
+
 template <typename T, int W>
 cudaError_t run_update(const UpdArgs& a, cudaStream_t stream) {
     constexpr int V = Vec<T>::V;
@@ -328,16 +368,10 @@ cudaError_t run_update(const UpdArgs& a, cudaStream_t stream) {
     }
     const bool lean = wvec && (a.bias == nullptr || bvec) && a.L == 1 && imode == kInterNone;
     if (xok && sok && iok && lean && (a.S == K || a.S == P) && a.B <= 65535) {
-        const int64_t nvec = a.D / V;
-        dim3 grid((unsigned)ceil_div(nvec, kUpdThreads), (unsigned)a.B);
-        if (a.status != nullptr) {
-            if (a.S == K) decode1_kernel<T, W, K, true><<<grid, kUpdThreads, 0, stream>>>(a);
-            else decode1_kernel<T, W, P, true><<<grid, kUpdThreads, 0, stream>>>(a);
-        } else {
-            if (a.S == K) decode1_kernel<T, W, K, false><<<grid, kUpdThreads, 0, stream>>>(a);
-            else decode1_kernel<T, W, P, false><<<grid, kUpdThreads, 0, stream>>>(a);
+        if constexpr (sizeof(T) == 2 && W <= 4) {
+            if (a.B >= 128) return launch_decode1<T, W, K, P, 2>(a, stream);
         }
-        return cudaGetLastError();
+        return launch_decode1<T, W, K, P, 1>(a, stream);
     }
     if (xok && sok && iok && a.L >= 1 && a.L <= 16 && a.B <= 65535) {
         if (a.S == K) {
