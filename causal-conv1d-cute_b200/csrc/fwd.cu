@@ -23,7 +23,6 @@ namespace {
 
 constexpr int kClThreads = 64;
 constexpr int kCfThreads = 256;
-constexpr int kCfElems = 16;  // elements per lane per iteration of the flat-stream kernel
 constexpr int kGenThreads = 256;
 
 template <typename T, int W, int U, bool PF, int NT>
@@ -87,18 +86,17 @@ __global__ void __launch_bounds__(NT, MINB)
     }
 }
 
-// Flat-stream kernel for contiguous (B, D, L) with L >= 16. Element f sits at row f / L (channel
+// Flat-stream kernel for contiguous (B, D, L) with L >= EPT. Element f sits at row f / L (channel
 // (f / L) % D) and position t = f % L; tap k of its output reads element f - (W-1) + k when that
-// lies in the same row (t >= W-1-k), zero otherwise. A lane owns EPT = 16 consecutive elements
-// (two 16-byte vectors for 16-bit types, four for fp32) and receives the W-1 elements before them
+// lies in the same row (t >= W-1-k), zero otherwise. A lane owns EPT (16 or 32, at most L)
+// consecutive elements (16-byte vectors) and receives the W-1 elements before them
 // from the lane to its left by a warp shuffle; lane 0 gets them from lane 31 of the previous
 // iteration, so every element is read from HBM once. The next iteration's vectors are requested
 // before the current ones are computed. A lane's elements straddle at most one row boundary.
-template <typename T, int W, bool V32>
+template <typename T, int W, bool V32, int EPT>
 __global__ void __launch_bounds__(kCfThreads)
     fwd_channel_first_kernel(const FwdArgs a, int64_t total, int iters) {
     constexpr int K = W - 1;
-    constexpr int EPT = kCfElems;
     constexpr int PER = 16 / (int)sizeof(T);
     constexpr int NV = EPT / PER;
     constexpr int WSPAN = 32 * EPT;  // elements per warp iteration
@@ -113,6 +111,8 @@ __global__ void __launch_bounds__(kCfThreads)
     const T* bs = (const T*)a.bias;
     const int64_t L = a.L, D = a.D;
     const bool use_silu = a.silu != 0;
+    // SiLU on a prescaled accumulator (walk.cuh: exactly half the sums, same outputs).
+    const float scale = (prescaled_silu<T>() && use_silu) ? 0.5f : 1.0f;
 
     int64_t f = base + lane * EPT;
     int64_t row = f / L;
@@ -169,6 +169,9 @@ __global__ void __launch_bounds__(kCfThreads)
         if (f < total) {
             if (c != wc) {
                 load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c, w0, b0);
+#pragma unroll
+                for (int k = 0; k < W; ++k) w0[k] *= scale;
+                b0 *= scale;
                 wc = c;
             }
             float o[EPT];
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(kCfThreads)
                     float acc = b0;
 #pragma unroll
                     for (int k = 0; k < W; ++k) acc = fmaf(win[e + k], w0[k], acc);
-                    o[e] = activate<T>(acc, use_silu);
+                    o[e] = activate_prescaled<T>(acc, use_silu);
                 }
                 if (V32) {
 #pragma unroll
@@ -204,6 +207,9 @@ __global__ void __launch_bounds__(kCfThreads)
                 if (straddle) {
                     const int64_t c1 = (c + 1 == D) ? 0 : c + 1;
                     load_filter1<T, W>(wt, a.w_sd, a.w_sk, bs, a.bias_s, c1, w1, b1);
+#pragma unroll
+                    for (int k = 0; k < W; ++k) w1[k] *= scale;
+                    b1 *= scale;
                 }
 #pragma unroll
                 for (int e = 0; e < EPT; ++e) {
@@ -215,7 +221,7 @@ __global__ void __launch_bounds__(kCfThreads)
                         const float v = (te >= K - k) ? win[e + k] : 0.f;
                         acc = fmaf(v, second ? w1[k] : w0[k], acc);
                     }
-                    o[e] = activate<T>(acc, use_silu);
+                    o[e] = activate_prescaled<T>(acc, use_silu);
                 }
                 if (full) {
 #pragma unroll
@@ -330,6 +336,50 @@ constexpr int share_min_ctas() {
     return W >= 5 ? 1 : 0;
 }
 
+// Elements per lane of the flat-stream kernel. 32 (four 16-byte vectors, 123-128 registers, two
+// CTAs per SM) halves the warp-shuffle halo and loop overhead per element against 16 (64-88
+// registers, three CTAs per SM). Measured on B200, bf16, 8192 channels, 16 -> 32 elements (us):
+// (8, 4096): W = 3: 220.2 -> 215.7 (1 x 40807), W = 4: 179.9 -> 175.5, W = 8: 193.5 -> 181.8
+// (204.0 before the prescaled SiLU), W = 2: 179.5 -> 174.8, W = 5: 184.6 -> 177.1, W = 6:
+// 186.8 -> 178.2; (1, 40807): W = 2: 220.5 -> 214.4, W = 4: 221.7 -> 216.9, W = 8: 238.8 ->
+// 225.6. W = 7 lost (189.5 -> 230.7) and keeps 16; W = 2 at 32 elements needs the cap of two
+// CTAs per SM (three: 197.8). Packed fp32x2 FMAs (__ffma2_rn, elements e and e + EPT/2 paired)
+// were slower at every width (W = 8, (8, 4096): 220.7 us at 16 elements) for their registers.
+template <typename T, int W>
+constexpr int cf_elems_per_lane() {
+    return sizeof(T) == 2 && W != 7 ? 32 : 16;
+}
+
+template <typename T, int W, int EPT>
+cudaError_t launch_channel_first(const FwdArgs& a, cudaStream_t stream) {
+    const int64_t total = a.B * a.D * a.L;
+    const int64_t chunks = ceil_div(total, 32 * EPT);  // one warp iteration each
+    // One wave: every resident warp walks an equal run of chunks (measured on B200 at the
+    // config-2 sizes, 16 elements per lane: 8 chunks per warp 196.5 us, 16: 189.8, 32: 188.1, one
+    // wave: 187.4). 32-byte accesses when both streams are 32-byte aligned (a lane's elements are).
+    const bool v32 = host_aligned32(a.x) && host_aligned32(a.out);
+    auto kern = v32 ? fwd_channel_first_kernel<T, W, true, EPT>
+                    : fwd_channel_first_kernel<T, W, false, EPT>;
+    static int slot_cache[2][kSlotCacheDevices] = {};
+    int64_t slots = std::max(1, device_slots((const void*)kern, kCfThreads, slot_cache[v32]));
+    // At most 3 resident CTAs per SM (the 16-bit kernels for W <= 4 at 16 elements fit 4).
+    // Measured on B200 (bf16, W = 4, 8192 channels, 16 elements; 4 -> 3 CTAs per SM, us):
+    // B x L = 1 x 20000: 126.8 -> 113.5; 1 x 40807: 243.6 -> 221.4; 1 x 65536: 381.5 -> 345.9;
+    // 8 x 4096: 199.1 -> 179.6; 4 x 8192: 198.7 -> 179.1; 16 x 2048: 193.5 -> 179.2;
+    // 2 x 16384: 197.2 -> 178.0; 8 x 7000: 314.8 -> 302.2; 6 x 5000: 165.8 -> 169.7 (the one
+    // shape of 14 that lost).
+    // With 32 elements per lane, at most 2 (the occupancy of every width but W = 2 anyway).
+    const int64_t cap = EPT == 32 ? 2 : 3;
+    const int sms = device_sm_count();
+    if (sms > 0 && slots > cap * sms) slots = cap * sms;
+    const int64_t wave_warps = slots * (kCfThreads / 32);
+    const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
+    const int64_t warps = ceil_div(chunks, iters);
+    const int64_t blocks = ceil_div(warps * 32, kCfThreads);
+    kern<<<(unsigned)blocks, kCfThreads, 0, stream>>>(a, total, iters);
+    return cudaGetLastError();
+}
+
 template <typename T, int W>
 cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     constexpr int V = Vec<T>::V;
@@ -365,29 +415,12 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     }
     const bool rows_dense = a.x_sl == 1 && a.o_sl == 1 && a.x_sd == a.L && a.o_sd == a.L &&
                             (a.B == 1 || (a.x_sb == a.D * a.L && a.o_sb == a.D * a.L));
-    if (rows_dense && a.L >= kCfElems && host_aligned16(a.x) && host_aligned16(a.out)) {
-        const int64_t total = a.B * a.D * a.L;
-        const int64_t chunks = ceil_div(total, 32 * kCfElems);  // one warp iteration each
-        // One wave: every resident warp walks an equal run of chunks (measured on B200 at the
-        // config-2 sizes: 8 chunks per warp 196.5 us, 16: 189.8, 32: 188.1, one wave: 187.4).
-        // 32-byte accesses when both streams are 32-byte aligned (a lane's 16 elements are).
-        const bool v32 = host_aligned32(a.x) && host_aligned32(a.out);
-        auto kern = v32 ? fwd_channel_first_kernel<T, W, true> : fwd_channel_first_kernel<T, W, false>;
-        static int slot_cache[2][kSlotCacheDevices] = {};
-        int64_t slots = std::max(1, device_slots((const void*)kern, kCfThreads, slot_cache[v32]));
-        // At most 3 resident CTAs per SM (the 16-bit kernels for W <= 4 fit 4). Measured on B200
-        // (bf16, W = 4, 8192 channels; 4 -> 3 CTAs per SM, us): B x L = 1 x 20000: 126.8 -> 113.5;
-        // 1 x 40807: 243.6 -> 221.4; 1 x 65536: 381.5 -> 345.9; 8 x 4096: 199.1 -> 179.6;
-        // 4 x 8192: 198.7 -> 179.1; 16 x 2048: 193.5 -> 179.2; 2 x 16384: 197.2 -> 178.0;
-        // 8 x 7000: 314.8 -> 302.2; 6 x 5000: 165.8 -> 169.7 (the one shape of 14 that lost).
-        const int sms = device_sm_count();
-        if (sms > 0 && slots > 3LL * sms) slots = 3LL * sms;
-        const int64_t wave_warps = slots * (kCfThreads / 32);
-        const int iters = (int)std::max<int64_t>(1, ceil_div(chunks, wave_warps));
-        const int64_t warps = ceil_div(chunks, iters);
-        const int64_t blocks = ceil_div(warps * 32, kCfThreads);
-        kern<<<(unsigned)blocks, kCfThreads, 0, stream>>>(a, total, iters);
-        return cudaGetLastError();
+    if (rows_dense && a.L >= 16 && host_aligned16(a.x) && host_aligned16(a.out)) {
+        // 32 elements per lane for 16-bit types on rows of 32+ elements (cf_elems_per_lane),
+        // else 16.
+        if (cf_elems_per_lane<T, W>() == 32 && a.L >= 32)
+            return launch_channel_first<T, W, cf_elems_per_lane<T, W>()>(a, stream);
+        return launch_channel_first<T, W, 16>(a, stream);
     }
     const int strip = 64;
     const int nstrips = (int)ceil_div(a.L, strip);

@@ -24,39 +24,56 @@ __global__ void __launch_bounds__(kUnpackThreads) unpack_kernel(const UnpackArgs
     const int64_t bi = blockIdx.y;
     const int64_t G = a.D / V, GZ = a.zdim / V;
     const T* qrow = (const T*)a.qkvz + bi * a.q_sb;
-    // The slot load heads the dependent chain (slot -> state): issue it before the copies.
+    // Every load that does not depend on the slot is issued before any store (a store waits for
+    // its data, so a copy placed first would hold back everything behind it): the slot, which
+    // heads the one dependent chain (slot -> state), then Z, B and A, x and the filter. Measured on
+    // B200 at the reference's sglang shape (10240 conv channels, 16384-column rows, 48 heads, bf16,
+    // L2 flushed before every call): B = 64 5.35 -> 4.56 us; B = 256 11.35 -> 10.82 us.
     const int32_t slot = j < G ? __ldg(a.idx + bi) : 0;
-    if (j < GZ) {
-        const uint4 zr = ldg16(qrow + a.D + j * V);
-        st16((T*)a.z + bi * a.zdim + j * V, zr);
-    }
+    uint4 zr;
+    if (j < GZ) zr = ldg16(qrow + a.D + j * V);
+    uint32_t bv = 0, av = 0;
+    const char* brow = (const char*)a.ba + bi * a.ba_sb * a.gsize;
     if (j < a.heads) {
-        const char* brow = (const char*)a.ba + bi * a.ba_sb * a.gsize;
-        const int64_t o = bi * a.heads + j;
         if (a.gsize == 4) {
-            reinterpret_cast<uint32_t*>(a.b)[o] = reinterpret_cast<const uint32_t*>(brow)[j];
-            reinterpret_cast<uint32_t*>(a.a)[o] =
-                reinterpret_cast<const uint32_t*>(brow)[a.heads + j];
+            bv = __ldg(reinterpret_cast<const uint32_t*>(brow) + j);
+            av = __ldg(reinterpret_cast<const uint32_t*>(brow) + a.heads + j);
         } else {
-            reinterpret_cast<uint16_t*>(a.b)[o] = reinterpret_cast<const uint16_t*>(brow)[j];
-            reinterpret_cast<uint16_t*>(a.a)[o] =
-                reinterpret_cast<const uint16_t*>(brow)[a.heads + j];
+            bv = __ldg(reinterpret_cast<const uint16_t*>(brow) + j);
+            av = __ldg(reinterpret_cast<const uint16_t*>(brow) + a.heads + j);
         }
     }
-    if (j >= G) return;
+    const bool conv = j < G;
     const int64_t c0 = j * V;
-    const uint4 xr = ldg16(qrow + c0);
+    uint4 xr, wt[W], bt;
+    if (conv) {
+        xr = ldg16(qrow + c0);
+        load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, bvec, wt, bt);
+    }
+    const bool live = conv && slot != a.pad && slot >= 0 && (int64_t)slot < a.nslots;
+    T* sp = (T*)a.state + (int64_t)slot * a.D * K + c0 * K;
+    uint4 blk[K];
+    if (live) {
+#pragma unroll
+        for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
+    }
+    if (j < GZ) st16((T*)a.z + bi * a.zdim + j * V, zr);
+    if (j < a.heads) {
+        const int64_t o = bi * a.heads + j;
+        if (a.gsize == 4) {
+            reinterpret_cast<uint32_t*>(a.b)[o] = bv;
+            reinterpret_cast<uint32_t*>(a.a)[o] = av;
+        } else {
+            reinterpret_cast<uint16_t*>(a.b)[o] = (uint16_t)bv;
+            reinterpret_cast<uint16_t*>(a.a)[o] = (uint16_t)av;
+        }
+    }
+    if (!conv) return;
     T* op = (T*)a.out + bi * a.D + c0;
-    if (slot == a.pad || slot < 0 || (int64_t)slot >= a.nslots) {
+    if (!live) {
         st16(op, xr);
         return;
     }
-    uint4 wt[W], bt;
-    load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, bvec, wt, bt);
-    T* sp = (T*)a.state + (int64_t)slot * a.D * K + c0 * K;
-    uint4 blk[K];
-#pragma unroll
-    for (int q = 0; q < K; ++q) blk[q] = ld16(sp + q * V);
     uint4 tm[K];
 #pragma unroll
     for (int e = 0; e < V; ++e)

@@ -155,3 +155,74 @@ def test_token_major_views_of_wider_rows(cols_extra):
     st = st0.clone()
     y = causal_conv1d_varlen_fn(xv, w, b, qsl, cidx, hinit, st, act, PAD)
     _check(y, st, x, w, b, act, qsl, cidx, hinit, st0)
+
+
+def _chunk_edge_lengths(T, chunk, K):
+    """Sequence lengths whose starts sit on, just before and just after warp-chunk edges of a
+    channel-first row (so heads cross chunk ends), plus an empty and a one-token sequence."""
+    starts = {0}
+    for edge in range(chunk, T, chunk):
+        for d in (-K, -K + 1, -1, 0, 1, K - 1):
+            if 0 < edge + d < T:
+                starts.add(edge + d)
+    starts = sorted(starts)
+    lens = [b - a for a, b in zip(starts, starts[1:] + [T])]
+    lens.insert(3, 0)
+    lens.insert(6, 1)
+    lens[-1] -= 1
+    return lens
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("W", [2, 4, 7, 8])
+def test_channel_first_matches_token_major(W, dtype):
+    """Contiguous (D, T) streams (stream pass + boundary launch) against token-major rows (one
+    launch): sequence starts on and around the stream kernel's warp-chunk edges, rows whose end
+    falls inside a chunk, an empty and a one-token sequence, a padding slot and sequences with and
+    without initial state. The outputs must equal each other bit for bit (the same arithmetic in
+    the same order) and the oracle's within tolerance; states bit-exact."""
+    torch.manual_seed(W)
+    K = W - 1
+    ept = 32 if dtype != torch.float32 and W != 7 else 16
+    D, T = 96, 3 * 32 * ept + 37
+    lens = _chunk_edge_lengths(T, 32 * ept, K)
+    nseq = len(lens)
+    qsl = torch.tensor([0] + list(np.cumsum(lens)), device="cuda", dtype=torch.int32)
+    slots = nseq + 3
+    cidx = torch.randperm(slots, device="cuda")[:nseq].to(torch.int32)
+    cidx[2] = PAD
+    hinit = torch.rand(nseq, device="cuda") < 0.5
+    hinit[0] = True
+    x = torch.randn(D, T, device="cuda", dtype=dtype)
+    w = torch.rand(D, W, device="cuda", dtype=dtype) - 0.5
+    b = torch.randn(D, device="cuda", dtype=dtype) * 0.1
+    st0 = torch.randn(slots, D, K, device="cuda", dtype=dtype)
+    st_cf, st_tm = st0.clone(), st0.clone()
+    y_cf = causal_conv1d_varlen_fn(x, w, b, qsl, cidx, hinit, st_cf, "silu", PAD)
+    y_tm = causal_conv1d_varlen_fn(x.t().contiguous().t(), w, b, qsl, cidx, hinit, st_tm, "silu",
+                                   PAD)
+    torch.cuda.synchronize()
+    assert torch.equal(st_cf, st_tm)
+    live = int(qsl[-1])
+    assert torch.equal(y_cf[:, :live], y_tm[:, :live])
+    from _util import TAG
+
+    r_out, r_st = oracle.varlen(to_np(x), to_np(w), to_np(b), to_np(qsl), to_np(cidx),
+                                to_np(hinit), to_np(st0), True, PAD, TAG[dtype])
+    mask = ~np.isnan(r_out)
+    assert_close(to_np(y_cf), np.nan_to_num(r_out), dtype, mask)
+    assert_bits(st_cf, r_st)
+
+
+@pytest.mark.gpu
+def test_channel_first_bad_bounds_are_clamped_and_reported(request):
+    request.node._expect_status = True
+    D, W, T = 64, 4, 3000
+    x = torch.randn(D, T, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(D, W, device="cuda", dtype=torch.bfloat16)
+    st = torch.randn(3, D, W - 1, device="cuda", dtype=torch.bfloat16)
+    qsl = torch.tensor([0, 1500, 1200, 90000], device="cuda", dtype=torch.int32)
+    device_status()
+    causal_conv1d_varlen_fn(x, w, None, qsl, None, None, st, None, PAD)
+    assert device_status() & 2
