@@ -983,6 +983,16 @@ def _profile_other(dev, g, width, case):
         qkvz = torch.randn(256, 16384, device=dev, generator=g).to(BF)
         ba = torch.randn(256, 96, device=dev, generator=g).to(BF)
         return lambda: U.causal_conv1d_update_unpack(qkvz, ba, st, wu, None, idx, 48, "silu", -1)
+    if case == "fwd_generic":  # config 2 at batch 2, token rows 3 elements wider than D
+        xw = torch.randn(2, L, D + 3, device=dev, generator=g).to(BF)
+        x = xw[:, :, :D].transpose(1, 2)
+        out = torch.empty(2, L, D, device=dev, dtype=BF).transpose(1, 2)
+        return lambda: C.causal_conv1d_fn(x, w, b, "silu", out=out)
+    if case == "update_generic":  # config 3 decode with x rows 3 elements wider than D
+        xw = torch.randn(256, D + 3, device=dev, generator=g).to(BF)
+        cache = torch.randn(1024, D, 3, device=dev, generator=g).to(BF)
+        idx = torch.randperm(1024, device=dev, generator=g)[:256].to(torch.int32)
+        return lambda: C.causal_conv1d_update(xw[:, :D], cache, w, b, "silu", idx)
     if case == "states":  # config 2 with batch 2, initial and final states
         x = torch.randn(2, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
         init = torch.randn(2, 3, D, device=dev, generator=g).to(BF).transpose(1, 2)
@@ -1009,6 +1019,8 @@ PROFILE_CASES = {
     "spec": lambda d, g, w: _profile_other(d, g, w, "spec"),
     "unpack": lambda d, g, w: _profile_other(d, g, w, "unpack"),
     "states": lambda d, g, w: _profile_other(d, g, w, "states"),
+    "fwd_generic": lambda d, g, w: _profile_other(d, g, w, "fwd_generic"),
+    "update_generic": lambda d, g, w: _profile_other(d, g, w, "update_generic"),
     "copy": lambda d, g, w: _profile_other(d, g, w, "copy"),
 }
 
