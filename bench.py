@@ -75,8 +75,9 @@ METRIC = "prefill/varlen achieved HBM GB/s vs ~8 TB/s; decode µs/call at bs=256
 B, L, D, W = 8, 4096, 8192, 4
 E = 2  # bf16
 HEADLINE_BYTES = 2 * B * L * D * E + D * W * E + D * E  # 1,073,823,744
-# The kernel the headline call dispatches to (balanced shares: W = 4, 4096-token sequences).
-HEADLINE_KERNEL = "fwd_channel_last_share_kernel"
+# The kernel the headline call dispatches to (16-bit channel-last prefill at W <= 5: 16-token
+# strips staged in shared memory, one per CTA).
+HEADLINE_KERNEL = "fwd_channel_last_staged_kernel"
 FLUSH_BYTES = 256 * 2**20  # twice L2 (126 MB)
 E2E_CHUNKS = 4  # token chunks per batch row in the e2e pipeline
 TOL = 1e-2  # bf16 output tolerance (atol = rtol)
@@ -125,7 +126,9 @@ def profiled_traffic(kernel):
 
 class ClockSampler:
     """Samples SM clock and clock-event reasons through NVML on a background thread, as fast as
-    NVML answers (period 0.5 ms), so that even a few-millisecond timed region gets samples."""
+    NVML answers (period 0.2 ms), so that even a few-millisecond timed region gets samples. It
+    runs from just before the first timed launch is enqueued (the warm-up has already been
+    synchronised) until the synchronize that closes the timed region, and keeps every sample."""
 
     REASONS = {
         "hw_slowdown": 0x8,
@@ -135,7 +138,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index, period=0.0005):
+    def __init__(self, device_index, period=0.0002):
         self.samples = []
         self.period = period
         self._stop = threading.Event()
@@ -166,8 +169,7 @@ class ClockSampler:
             try:
                 mhz = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
                 reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                util = n.nvmlDeviceGetUtilizationRates(self.handle).gpu
-                self.samples.append((mhz, reasons, util))
+                self.samples.append((mhz, reasons))
             except Exception:  # noqa: BLE001
                 pass
             time.sleep(self.period)
@@ -186,7 +188,7 @@ class ClockSampler:
     def summary(self):
         if not self.ok:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.error}
-        busy = [s for s in self.samples if s[2] > 0] or self.samples
+        busy = self.samples
         mhz = [s[0] for s in busy]
         seen = set()
         for s in busy:

@@ -181,6 +181,21 @@ __device__ __forceinline__ void st16_stream(void* p, const uint4& v) {
                  : "memory");
 }
 
+// Asynchronous 16-byte copy global -> shared (cached in L2 only), and its group fences. The bytes
+// in flight hold no registers: a thread waits for its own copies with cp_async_wait<N>() (at most
+// N of its committed groups still pending) and then reads them from shared memory.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // A thread's channel vector of NB bytes (16: uint4, 8: uint2) for the kernels that can run with
 // half-width vectors (fewer registers per thread when the filter is wide).
 template <int NB>

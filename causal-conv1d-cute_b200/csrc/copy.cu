@@ -4,9 +4,12 @@
 // and written once, with the widest accesses sm_100 has (32-byte vectors), so the gap between a
 // kernel and this copy is what the kernel's own work costs.
 //
-// copy_kernel: one wave of CTAs; warp w walks a contiguous run of 32-byte chunks, every lane
-// keeping U chunks in flight (all U loads issued before the first store), so the loads of a warp
-// cover U * 1 KB of consecutive bytes. A tail that is not a whole chunk is copied byte by byte.
+// copy_kernel: one tile of kCopyThreads x kCopyUnroll 32-byte chunks per CTA, every thread
+// issuing its kCopyUnroll loads before its stores, and as many CTAs as tiles: the hardware runs them
+// in waves, so the bytes requested at any moment lie in a narrow window of consecutive tiles.
+// Measured on B200 with 512 MiB in and out: 162.2 us with one tile of 2 chunks per thread, against
+// 172.0 us for cudaMemcpyAsync and 184-186 us for a single wave of CTAs each walking a long run
+// (per-warp runs or a grid-stride loop). A tail that is not a whole chunk is copied byte by byte.
 #include <algorithm>
 
 #include "common.cuh"
@@ -17,30 +20,25 @@ namespace cc1d {
 namespace {
 
 constexpr int kCopyThreads = 256;
-constexpr int kCopyUnroll = 4;
+constexpr int kCopyUnroll = 2;
 
 __global__ void __launch_bounds__(kCopyThreads)
     copy_kernel(uint8_t* __restrict__ dst, const uint8_t* __restrict__ src, int64_t chunks,
-                int64_t per_warp, int64_t bytes) {
-    const int lane = threadIdx.x & 31;
-    const int64_t warp = ((int64_t)blockIdx.x * kCopyThreads + threadIdx.x) >> 5;
-    const int64_t c0 = warp * per_warp;
-    const int64_t c1 = c0 + per_warp < chunks ? c0 + per_warp : chunks;
-    for (int64_t c = c0; c < c1; c += 32 * kCopyUnroll) {
-        uint4 lo[kCopyUnroll], hi[kCopyUnroll];
+                int64_t bytes) {
+    const int64_t k0 = (int64_t)blockIdx.x * kCopyThreads * kCopyUnroll + threadIdx.x;
+    uint4 lo[kCopyUnroll], hi[kCopyUnroll];
 #pragma unroll
-        for (int u = 0; u < kCopyUnroll; ++u) {
-            const int64_t k = c + u * 32 + lane;
-            if (k < c1) ldg32_stream(src + k * 32, lo[u], hi[u]);
-        }
-#pragma unroll
-        for (int u = 0; u < kCopyUnroll; ++u) {
-            const int64_t k = c + u * 32 + lane;
-            if (k < c1) st32_stream(dst + k * 32, lo[u], hi[u]);
-        }
+    for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t k = k0 + u * kCopyThreads;
+        if (k < chunks) ldg32_stream(src + k * 32, lo[u], hi[u]);
     }
-    if (warp == 0) {
-        for (int64_t i = chunks * 32 + lane; i < bytes; i += 32) dst[i] = src[i];
+#pragma unroll
+    for (int u = 0; u < kCopyUnroll; ++u) {
+        const int64_t k = k0 + u * kCopyThreads;
+        if (k < chunks) st32_stream(dst + k * 32, lo[u], hi[u]);
+    }
+    if (blockIdx.x == 0 && threadIdx.x < 32) {
+        for (int64_t i = chunks * 32 + threadIdx.x; i < bytes; i += 32) dst[i] = src[i];
     }
 }
 
@@ -49,16 +47,11 @@ __global__ void __launch_bounds__(kCopyThreads)
 cudaError_t launch_copy(void* dst, const void* src, int64_t bytes, cudaStream_t stream) {
     if (bytes <= 0) return cudaSuccess;
     const int64_t chunks = bytes / 32;
-    static int slot_cache[kSlotCacheDevices] = {};
-    const int64_t slots = std::max(1, device_slots((const void*)copy_kernel, kCopyThreads, slot_cache));
-    const int64_t warps_wave = slots * (kCopyThreads / 32);
-    // Runs a whole number of warp steps (32 lanes x U chunks) long, one wave of warps in total.
-    const int64_t step = 32 * kCopyUnroll;
-    const int64_t per_warp = std::max<int64_t>(step, ceil_div(ceil_div(chunks, warps_wave), step) * step);
-    const int64_t warps = std::max<int64_t>(1, ceil_div(chunks, per_warp));
-    const int64_t blocks = ceil_div(warps * 32, (int64_t)kCopyThreads);
+    const int64_t blocks =
+        std::max<int64_t>(1, ceil_div(chunks, (int64_t)kCopyThreads * kCopyUnroll));
+    if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     copy_kernel<<<(unsigned)blocks, kCopyThreads, 0, stream>>>((uint8_t*)dst, (const uint8_t*)src,
-                                                               chunks, per_warp, bytes);
+                                                               chunks, bytes);
     return cudaGetLastError();
 }
 

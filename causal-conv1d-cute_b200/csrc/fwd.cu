@@ -1,15 +1,18 @@
 // Prefill over dense batched sequences (replaces causal_conv1d_cute/fwd.py).
 //
-// Three kernels, chosen by layout in launch_fwd:
-//   fwd_channel_last   (B, L, D) storage, token rows of D adjacent channels (x_sd == 1): every
-//                      thread owns one 16-byte vector of channels and walks a run of tokens,
-//                      keeping the W-1 most recent inputs in registers; a run re-reads only the
-//                      W-1 rows before it, which its neighbour has just pulled into L2. Runs are
-//                      fixed strips (several waves) or balanced shares (one wave), per the launch
-//                      table in run_fwd.
+// Kernels, chosen by layout and width in run_fwd:
+//   fwd_channel_last_staged  (B, L, D) storage, 16-bit types, W <= 5: one CTA per strip of 16
+//                      tokens of one batch row and 64 16-byte channel vectors; each thread lands
+//                      its column of the strip (and the W-1 rows before it) in shared memory with
+//                      cp.async and walks it there. Many short-lived CTAs, several waves.
+//   fwd_channel_last   (B, L, D) storage otherwise (x_sd == 1): every thread owns one 16-byte (or
+//   _share             8-byte) vector of channels and walks a run of tokens from registers,
+//                      keeping the W-1 most recent inputs; a run re-reads only the W-1 rows
+//                      before it, which its neighbour has just pulled into L2. Runs are fixed
+//                      strips (several waves) or balanced shares (one wave), per the launch table.
 //   fwd_channel_first  (B, D, L) contiguous storage: the tensor is one flat stream; every lane of
-//                      a warp owns 8 consecutive elements and receives the W-1 elements before
-//                      them from the lane to its left by a warp shuffle, so HBM is read once.
+//                      a warp owns 16 or 32 consecutive elements and receives the W-1 elements
+//                      before them from the lane to its left by a warp shuffle, so HBM is read once.
 //   fwd_generic        any other strides, one channel per thread (correctness path).
 #include <algorithm>
 
@@ -84,6 +87,89 @@ __global__ void __launch_bounds__(NT, MINB)
         walk_strip<T, W, U, PF, NB>(xb, a.x_sl, ob, a.o_sl, t0, t0 + n, h, w, bv, use_silu);
         r += n;
     }
+}
+
+// One strip of n rows (n == S when FULL): copies, filter, then the walk from shared memory. The
+// full-strip form has no per-row guard, so the window shift of every row is a static register
+// renaming; a guard on each row turns it into a select per window register (the W = 4 kernel took
+// 243 instead of 164 us at the config-2 shape that way), so only a batch row's last strip, when
+// L is not a multiple of S, takes the guarded form.
+template <typename T, int W, int S, int NT, bool FULL>
+__device__ __forceinline__ void staged_strip(const FwdArgs& a, uint4* col, const T* xb, T* ob,
+                                             int64_t t0, int64_t n, int64_t c0, bool wvec,
+                                             bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    constexpr int HALF = S / 2;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int64_t t = t0 - K + k;
+        if (t >= 0) cp_async16(col + k * NT, xb + t * a.x_sl);
+        else col[k * NT] = make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int i = 0; i < HALF; ++i)
+        if (FULL || i < n) cp_async16(col + (K + i) * NT, xb + (t0 + i) * a.x_sl);
+    cp_async_commit();
+#pragma unroll
+    for (int i = HALF; i < S; ++i)
+        if (FULL || i < n) cp_async16(col + (K + i) * NT, xb + (t0 + i) * a.x_sl);
+    cp_async_commit();
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = a.silu != 0;
+    prescale_filter<T, W>(w, bv, use_silu);
+    float h[K][V];
+    auto row = [&](int r) {
+        float xv[V], o[V];
+        unpack16<T>(col[(K + r) * NT], xv);
+        conv_step<T, W>(h, xv, w, bv, use_silu, o);
+        st16_stream(ob + (t0 + r) * a.o_sl, pack16<T>(o));
+    };
+    cp_async_wait<1>();
+#pragma unroll
+    for (int k = 0; k < K; ++k) unpack16<T>(col[k * NT], h[k]);
+    if (FULL) {
+#pragma unroll
+        for (int r = 0; r < HALF; ++r) row(r);
+        cp_async_wait<0>();
+#pragma unroll
+        for (int r = HALF; r < S; ++r) row(r);
+    } else {
+        cp_async_wait<0>();
+        for (int r = 0; r < n; ++r) row(r);
+    }
+}
+
+// Staged variant, one short strip per CTA: blockIdx.x = strip * gx + channel block, where a strip
+// is S consecutive tokens of one batch row and a channel block NT 16-byte vectors. Each thread
+// copies its own 16-byte column of the W-1 rows before the strip and of the strip's S rows into
+// shared memory with cp.async (the bytes in flight hold no registers), loads the filter while
+// they land, waits for its own copies (in two groups: the first half is computed while the second
+// lands) and walks the rows from shared memory. No thread reads another's column, so there is no
+// barrier. The grid runs many short-lived CTAs back to back, which keeps the bytes requested from
+// DRAM at any moment within a narrow window of consecutive rows, as a copy does; the halo rows
+// were just read by the neighbouring strip's CTA and come from L2.
+template <typename T, int W, int S, int NT>
+__global__ void __launch_bounds__(NT)
+    fwd_channel_last_staged_kernel(const FwdArgs a, int64_t nstrips, int64_t gx, bool wvec,
+                                   bool bvec) {
+    constexpr int V = Vec<T>::V;
+    extern __shared__ uint4 stage[];
+    const int64_t blk = blockIdx.x;
+    const int64_t su = blk / gx;
+    const int64_t j = (blk - su * gx) * NT + threadIdx.x;
+    if (j >= a.D / V) return;
+    const int64_t b = su / nstrips;
+    const int64_t t0 = (su - b * nstrips) * S;
+    const int64_t n = min((int64_t)S, a.L - t0);
+    const int64_t c0 = j * V;
+    const T* xb = (const T*)a.x + b * a.x_sb + c0;
+    T* ob = (T*)a.out + b * a.o_sb + c0;
+    uint4* col = stage + threadIdx.x;  // row r of the stage (halo rows first) at col[r * NT]
+    if (n == S) staged_strip<T, W, S, NT, true>(a, col, xb, ob, t0, n, c0, wvec, bvec);
+    else staged_strip<T, W, S, NT, false>(a, col, xb, ob, t0, n, c0, wvec, bvec);
 }
 
 // Flat-stream kernel for contiguous (B, D, L) with L >= EPT. Element f sits at row f / L (channel
@@ -336,6 +422,23 @@ constexpr int share_min_ctas() {
     return W >= 5 ? 1 : 0;
 }
 
+// The staged walk (one 16-token strip per 64-thread CTA, rows landed in shared memory by
+// cp.async) serves 16-bit types up to W = 5. Measured on B200 at the config-2 shape (8 x 4096 x
+// 8192 bf16, one launch at a time; staged vs the register walk above, us): W = 2: 163.0 vs 174.1;
+// 3: 165.3 vs 176.6; 4: 163.7 vs 184.1; 5: 165.5 vs 185.5. The copy of the same bytes takes
+// 162-164 us. Longer strips lost (W = 4: 32 tokens 175.7 us, 64: 256.5 us: fewer CTAs fit and
+// each lives longer), as did the same strips walked from registers (16 tokens, all loads up front:
+// 210 us at W = 4, spilling) and with one-thread bulk copies of whole 1 KB row segments on an
+// mbarrier (164.8 us, no gain). From W = 6 the filter and window of a 16-byte vector leave too
+// few CTAs per SM and the 8-byte form re-reads a relatively longer halo (W = 8: 226-237 us
+// against 199 us for the register walk), so wide filters and fp32 keep the register walk.
+constexpr int kStageRows = 16;
+constexpr int kStageThreads = 64;
+template <typename T, int W>
+constexpr bool staged_prefill() {
+    return sizeof(T) == 2 && W <= 5;
+}
+
 // Elements per lane of the flat-stream kernel. 32 (four 16-byte vectors, 123-128 registers, two
 // CTAs per SM) halves the warp-shuffle halo and loop overhead per element against 16 (64-88
 // registers, three CTAs per SM). Measured on B200, bf16, 8192 channels, 16 -> 32 elements (us):
@@ -391,6 +494,18 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
                     (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0;
     if (cl) {
         const int64_t nvec = a.D / V;
+        if constexpr (staged_prefill<T, W>()) {
+            const int64_t sgx = ceil_div(nvec, (int64_t)kStageThreads);
+            const int64_t nstrips = ceil_div(a.L, (int64_t)kStageRows);
+            const int64_t blocks = sgx * a.B * nstrips;
+            if (blocks <= 0x7fffffffLL) {
+                const size_t smem = (size_t)(kStageRows + W - 1) * kStageThreads * 16;
+                fwd_channel_last_staged_kernel<T, W, kStageRows, kStageThreads>
+                    <<<(unsigned)blocks, kStageThreads, smem, stream>>>(a, nstrips, sgx, wvec,
+                                                                        bvec);
+                return cudaGetLastError();
+            }
+        }
         const int64_t gx = ceil_div(nvec, (int64_t)kClThreads);
         constexpr int SB = share_bytes<T, W>();
         constexpr int SNT = share_threads<T, W>();
