@@ -261,7 +261,7 @@ class Flusher:
         self.buf.fill_(1)
 
 
-def cold_warm_us(call, flush, n=20, rounds=5):
+def cold_warm_us(call, flush, n=20, rounds=9):
     """Per-call microseconds of a decode-sized call: cold (L2 flushed before every call) and warm.
 
     cold = (graph of n x [flush, call] - graph of n x [flush]) / n, median over rounds: the call's

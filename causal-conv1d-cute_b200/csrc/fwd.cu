@@ -101,20 +101,10 @@ __device__ __forceinline__ void staged_strip(const FwdArgs& a, uint4* col, const
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     constexpr int HALF = S / 2;
+    stage_strip<T, K, S, NT, FULL>(col, xb, a.x_sl, t0, n);
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-        const int64_t t = t0 - K + k;
-        if (t >= 0) cp_async16(col + k * NT, xb + t * a.x_sl);
-        else col[k * NT] = make_uint4(0u, 0u, 0u, 0u);
-    }
-#pragma unroll
-    for (int i = 0; i < HALF; ++i)
-        if (FULL || i < n) cp_async16(col + (K + i) * NT, xb + (t0 + i) * a.x_sl);
-    cp_async_commit();
-#pragma unroll
-    for (int i = HALF; i < S; ++i)
-        if (FULL || i < n) cp_async16(col + (K + i) * NT, xb + (t0 + i) * a.x_sl);
-    cp_async_commit();
+    for (int k = 0; k < K; ++k)
+        if (t0 - K + k < 0) col[k * NT] = make_uint4(0u, 0u, 0u, 0u);
     float w[W][V], bv[V];
     load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
                       w, bv);
@@ -424,9 +414,10 @@ constexpr int share_min_ctas() {
 
 // The staged walk (one 16-token strip per 64-thread CTA, rows landed in shared memory by
 // cp.async) serves 16-bit types up to W = 5. Measured on B200 at the config-2 shape (8 x 4096 x
-// 8192 bf16, one launch at a time; staged vs the register walk above, us): W = 2: 163.0 vs 174.1;
-// 3: 165.3 vs 176.6; 4: 163.7 vs 184.1; 5: 165.5 vs 185.5. The copy of the same bytes takes
-// 162-164 us. Longer strips lost (W = 4: 32 tokens 175.7 us, 64: 256.5 us: fewer CTAs fit and
+// 8192 bf16, one launch at a time; staged vs the register walk above, us): W = 2: 161.7 vs 174.1;
+// 3: 166.3 vs 176.6; 4: 165.4 vs 184.1; 5: 183.6 vs 185.5. The library's copy of the same bytes
+// takes 160-161 us. A minimum of 10-12 resident CTAs in the launch bounds gained nothing at
+// W <= 4 and made W = 5 slower (242 us), since it caps registers below what the walk needs. Longer strips lost (W = 4: 32 tokens 175.7 us, 64: 256.5 us: fewer CTAs fit and
 // each lives longer), as did the same strips walked from registers (16 tokens, all loads up front:
 // 210 us at W = 4, spilling) and with one-thread bulk copies of whole 1 KB row segments on an
 // mbarrier (164.8 us, no gain). From W = 6 the filter and window of a 16-byte vector leave too
@@ -438,6 +429,7 @@ template <typename T, int W>
 constexpr bool staged_prefill() {
     return sizeof(T) == 2 && W <= 5;
 }
+
 
 // Elements per lane of the flat-stream kernel. 32 (four 16-byte vectors, 123-128 registers, two
 // CTAs per SM) halves the warp-shuffle halo and loop overhead per element against 16 (64-88

@@ -10,12 +10,15 @@
 // multiplied by zero). final[b, c, k] = the k-th of the last W-1 entries of [init[b, c, :] | x[b, c, :]]
 // (zeros in place of init without initial states), copied bit for bit from the inputs.
 //
-// Two kernels:
-//   fwd_states_vec_kernel   channel-last x / out (16-byte channel vectors, the walk and grid of
-//                           the plain channel-last prefill): a thread walks a share of token
-//                           rows of one 16-byte channel group; a stretch that starts a row takes
-//                           its history from the initial states, the one that ends it writes the
-//                           final states.
+// Kernels:
+//   fwd_states_staged_kernel  channel-last x / out, 16-bit types, W <= 5, no sequence ids: the
+//                           staged 16-token strips of the plain prefill (one per CTA, landed in
+//                           shared memory), initial states in the halo of a row's first strip.
+//   fwd_states_vec_kernel   channel-last x / out otherwise (16-byte channel vectors, the walk and
+//                           grid of the plain channel-last register walk): a thread walks a share
+//                           of token rows of one 16-byte channel group; a stretch that starts a
+//                           row takes its history from the initial states, the one that ends it
+//                           writes the final states.
 //   fwd_states_generic_kernel  any strides, one channel of a strip per thread.
 #include <algorithm>
 
@@ -130,6 +133,85 @@ __global__ void __launch_bounds__(kStThreads)
     }
 }
 
+// Staged form for 16-bit types up to W = 5 (the launch table of the plain prefill, fwd.cu): one
+// CTA per strip of S tokens of one batch row and NT channel vectors, the strip landed in shared
+// memory by cp.async (stage_strip). History before token 0 is the initial states (zeros without
+// them), written into the stage's halo rows; the strip that ends a row writes that row's final
+// states. Calls with sequence ids keep the register walk (see the launch table). FULL: a whole
+// strip of S rows (no per-row guard, see the plain staged kernel).
+template <typename T, int W, int S, int NT, bool FULL>
+__device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, int64_t b,
+                                             int64_t t0, int64_t n, int64_t c0, bool wvec,
+                                             bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    constexpr int HALF = S / 2;
+    const FwdArgs& f = a.f;
+    const T* xb = (const T*)f.x + b * f.x_sb + c0;
+    stage_strip<T, K, S, NT, FULL>(col, xb, f.x_sl, t0, n);
+    const T* init = (const T*)a.init;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int64_t t = t0 - K + k;
+        if (t < 0) {
+            uint4 v = make_uint4(0u, 0u, 0u, 0u);
+            if (init != nullptr) {
+#pragma unroll
+                for (int e = 0; e < V; ++e)
+                    set_lane<T>(v, e, init[b * a.i_sb + (c0 + e) * a.i_sd + (K + t) * a.i_sk]);
+            }
+            col[k * NT] = v;
+        }
+    }
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)f.w, f.w_sd, f.w_sk, (const T*)f.bias, f.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = f.silu != 0;
+    prescale_filter<T, W>(w, bv, use_silu);
+    T* ob = (T*)f.out + b * f.o_sb + c0;
+    float h[K][V];
+    auto row = [&](int r) {
+        float xv[V], o[V];
+        unpack16<T>(col[(K + r) * NT], xv);
+        conv_step<T, W>(h, xv, w, bv, use_silu, o);
+        st16_stream(ob + (t0 + r) * f.o_sl, pack16<T>(o));
+    };
+    cp_async_wait<1>();
+#pragma unroll
+    for (int k = 0; k < K; ++k) unpack16<T>(col[k * NT], h[k]);
+    if (FULL) {
+#pragma unroll
+        for (int r = 0; r < HALF; ++r) row(r);
+        cp_async_wait<0>();
+#pragma unroll
+        for (int r = HALF; r < S; ++r) row(r);
+    } else {
+        cp_async_wait<0>();
+#pragma unroll
+        for (int r = 0; r < S; ++r)
+            if (r < n) row(r);
+    }
+    if (a.fin != nullptr && t0 + n == f.L) states_final<T, W>(a, b, c0, V);
+}
+
+template <typename T, int W, int S, int NT>
+__global__ void __launch_bounds__(NT)
+    fwd_states_staged_kernel(const FwdStateArgs a, int64_t nstrips, int64_t gx, bool wvec,
+                             bool bvec) {
+    constexpr int V = Vec<T>::V;
+    extern __shared__ uint4 stage[];
+    const int64_t blk = blockIdx.x;
+    const int64_t su = blk / gx;
+    const int64_t j = (blk - su * gx) * NT + threadIdx.x;
+    if (j >= a.f.D / V) return;
+    const int64_t b = su / nstrips;
+    const int64_t t0 = (su - b * nstrips) * S;
+    const int64_t n = min((int64_t)S, a.f.L - t0);
+    uint4* col = stage + threadIdx.x;
+    if (n == S) states_strip<T, W, S, NT, true>(a, col, b, t0, n, j * V, wvec, bvec);
+    else states_strip<T, W, S, NT, false>(a, col, b, t0, n, j * V, wvec, bvec);
+}
+
 // Any strides: thread = (row, channel, strip of kStStrip tokens).
 template <typename T, int W>
 __global__ void __launch_bounds__(kStGenThreads) fwd_states_generic_kernel(const FwdStateArgs a,
@@ -207,6 +289,23 @@ cudaError_t run_fwd_states(const FwdStateArgs& a, cudaStream_t stream) {
     const bool cl = f.x_sd == 1 && f.o_sd == 1 && f.D % V == 0 && host_aligned16(f.x) &&
                     host_aligned16(f.out) && (f.x_sl * e) % 16 == 0 && (f.o_sl * e) % 16 == 0 &&
                     (f.x_sb * e) % 16 == 0 && (f.o_sb * e) % 16 == 0;
+    if constexpr (sizeof(T) == 2 && W <= 5) {
+        // Staged 16-token strips, one per 64-thread CTA, as the plain channel-last prefill.
+        // Measured on B200 at the config-2 shape (bf16, W = 4), staged vs the balanced register
+        // walk below: initial + final states 172.5 vs 182.9 us; with sequence ids 183.4 vs
+        // 181.3 us (the per-row ids and masked taps cost more than staging saves), so calls with
+        // sequence ids keep the register walk.
+        constexpr int S = 16, NT = 64;
+        const int64_t gx = ceil_div(f.D / V, (int64_t)NT);
+        const int64_t strips = ceil_div(f.L, (int64_t)S);
+        const int64_t blocks = gx * f.B * strips;
+        if (cl && f.L > 0 && a.seq == nullptr && blocks <= 0x7fffffffLL) {
+            const size_t smem = (size_t)(S + W - 1) * NT * 16;
+            fwd_states_staged_kernel<T, W, S, NT>
+                <<<(unsigned)blocks, NT, smem, stream>>>(a, strips, gx, wvec, bvec);
+            return cudaGetLastError();
+        }
+    }
     if (cl) {
         // Launch table as for the plain channel-last prefill (fwd.cu): many ~128-row shares,
         // balanced by the block scheduler, for W <= 3 or short sequences when they give at least

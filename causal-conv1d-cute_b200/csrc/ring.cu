@@ -3,7 +3,7 @@
 // The ring state (slots, W-1, D) keeps the last W-1 inputs of a sequence unordered: row
 // seen % (W-1) holds the oldest. A step reads the W-1 rows and x, writes the output and
 // overwrites only the oldest row with x, so it stores one state row instead of W-1. Each thread
-// owns a 16-byte vector of channels of one batch row. The rows are already time-major vectors;
+// owns a vector of channels (8 bytes for 16-bit types, 16 for fp32) of R batch rows. The rows are already time-major vectors;
 // tap k (oldest first) takes row (pos + k) % (W-1), picked from registers by a select chain so
 // that the weight loads never wait on the sequence length. The taps are summed oldest first, the
 // order of the ordered-state decode, so both layouts give identical outputs.
@@ -28,58 +28,78 @@ __device__ __forceinline__ int ring_pos(int32_t seen, int K) {
     return p < 0 ? p + K : p;
 }
 
-template <typename T, int W>
+// R batch rows per thread (gridDim.y == ceil(B / R)) and NB bytes of channels per thread; raw
+// weights widened at use. Every load of every row is issued before any compute: the slot and
+// count loads first (each heads the only dependent chain, slot -> ring rows), then the filter and
+// the x rows, then the ring rows.
+template <typename T, int W, int NB, int R>
 __global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bool wvec, bool bvec) {
-    constexpr int V = Vec<T>::V;
+    using RV = typename RawVec<NB>::type;
+    constexpr int V = NB / (int)sizeof(T);
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
     const int64_t j = (int64_t)blockIdx.x * kRingThreads + threadIdx.x;
     if (j >= nvec) return;
     const int64_t c0 = j * V;
-    // One row per thread (gridDim.y == B) and raw weights widened at use: a lean thread keeps
-    // twice as many of them resident.
-    const int64_t b = blockIdx.y;
-    // The slot load heads the dependent chain (slot -> ring rows): issue it first.
-    const int32_t slot = a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b;
-    const int32_t seen = __ldg(a.seen + b);
-    uint4 wt[W], bt;
+    int32_t slot[R], seen[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t b = (int64_t)blockIdx.y * R + r;
+        slot[r] = b < a.B ? (a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b) : a.pad;
+        seen[r] = b < a.B ? __ldg(a.seen + b) : 0;
+    }
+    RV wt[W], bt;
     load_filter_raw<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
                           bvec, wt, bt);
-    const uint4 xr = ldg16((const T*)a.x + b * a.x_sb + c0);
-    const int pos = ring_pos(seen, K);
-    if (slot == a.pad) return;
-    if (slot < 0 || (int64_t)slot >= a.nslots) {
-        if (j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
-        return;
+    RV xr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t b = (int64_t)blockIdx.y * R + r;
+        if (b < a.B) xr[r] = ldg_raw<NB>((const T*)a.x + b * a.x_sb + c0);
     }
-    T* rb = (T*)a.ring + (int64_t)slot * a.r_slot + c0;
-    uint4 rows[K];
+    bool live[R];
+    RV rows[R][K];
 #pragma unroll
-    for (int q = 0; q < K; ++q) rows[q] = ld16(rb + q * a.r_sk);
-    float acc[V];
-    unpack16<T>(bt, acc);
+    for (int r = 0; r < R; ++r) {
+        live[r] = slot[r] != a.pad && slot[r] >= 0 && (int64_t)slot[r] < a.nslots;
+        if (!live[r] && slot[r] != a.pad && j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
+        if (live[r]) {
+            const T* rb = (const T*)a.ring + (int64_t)slot[r] * a.r_slot + c0;
 #pragma unroll
-    for (int k = 0; k < K; ++k) {
-        int r = pos + k;
-        r = r >= K ? r - K : r;
-        uint4 v = rows[0];
-#pragma unroll
-        for (int q = 1; q < K; ++q) v = (r == q) ? rows[q] : v;
-        float f[V], wk[V];
-        unpack16<T>(v, f);
-        unpack16<T>(wt[k], wk);
-#pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
+            for (int q = 0; q < K; ++q) rows[r][q] = ld_raw<NB>(rb + q * a.r_sk);
+        }
     }
-    {
-        float f[V], wk[V];
-        unpack16<T>(xr, f);
-        unpack16<T>(wt[K], wk);
 #pragma unroll
-        for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), a.silu != 0);
+    for (int r = 0; r < R; ++r) {
+        if (!live[r]) continue;
+        const int64_t b = (int64_t)blockIdx.y * R + r;
+        const int pos = ring_pos(seen[r], K);
+        float acc[V];
+        unpack_raw<T, NB>(bt, acc);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            int p = pos + k;
+            p = p >= K ? p - K : p;
+            RV v = rows[r][0];
+#pragma unroll
+            for (int q = 1; q < K; ++q) v = (p == q) ? rows[r][q] : v;
+            float f[V], wk[V];
+            unpack_raw<T, NB>(v, f);
+            unpack_raw<T, NB>(wt[k], wk);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
+        }
+        {
+            float f[V], wk[V];
+            unpack_raw<T, NB>(xr[r], f);
+            unpack_raw<T, NB>(wt[K], wk);
+#pragma unroll
+            for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), a.silu != 0);
+        }
+        T* rb = (T*)a.ring + (int64_t)slot[r] * a.r_slot + c0;
+        st_raw<NB>(rb + pos * a.r_sk, xr[r]);
+        st_raw<NB>((T*)a.out + b * a.o_sb + c0, pack_raw<T, NB>(acc));
     }
-    st16(rb + pos * a.r_sk, xr);
-    st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
 }
 
 template <typename T, int W>
@@ -125,9 +145,23 @@ cudaError_t run_ring(const RingArgs& a, cudaStream_t stream) {
                      (a.x_sb * e) % 16 == 0 && (a.o_sb * e) % 16 == 0 &&
                      (a.r_slot * e) % 16 == 0 && (a.r_sk * e) % 16 == 0;
     if (vec && a.B <= 65535) {
+        // 16-bit types: 4 channels per thread (8-byte vectors), 2 rows per thread below 128 rows
+        // and 4 from 128 rows, as the lean decode. Measured on B200 (D = 8192, bf16, W = 4, CUDA
+        // graphs, 256 MiB L2 flush before every call; cold / warm us, as (NB bytes, R rows), one
+        // run): B = 64: (16, 1) 4.52 / 3.07, (8, 1) 4.10 / 3.01, (8, 2) 3.97 / 2.84,
+        // (8, 4) 4.12 / 2.92; B = 256: (16, 1) 8.64 / 6.32, (8, 2) 7.72 / 5.79, (8, 4) 7.18 / 5.00,
+        // (16, 4) 8.34 / 5.22. fp32 keeps one row of 16-byte vectors.
+        if constexpr (sizeof(T) == 2) {
+            const int64_t nvec8 = a.D / (8 / (int64_t)sizeof(T));
+            const int R = a.B >= 128 ? 4 : 2;
+            dim3 grid((unsigned)ceil_div(nvec8, kRingThreads), (unsigned)ceil_div(a.B, (int64_t)R));
+            if (R == 4) ring_kernel<T, W, 8, 4><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
+            else ring_kernel<T, W, 8, 2><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
+            return cudaGetLastError();
+        }
         const int64_t nvec = a.D / V;
         dim3 grid((unsigned)ceil_div(nvec, kRingThreads), (unsigned)a.B);
-        ring_kernel<T, W><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
+        ring_kernel<T, W, 16, 1><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     const int64_t n = a.B * a.D;

@@ -157,27 +157,32 @@ __global__ void __launch_bounds__(kUpdThreads)
 }
 
 // Single-step decode without per-step states, the serving hot case, kept lean: R batch rows per
-// thread (gridDim.y == ceil(B / R)), raw tap-major weights widened at use, no runtime step loop
-// (the general kernel's 90 registers halve the resident threads). Every load is issued before any
-// compute: the slot loads first, since each heads the only dependent chain (slot -> state), then
-// the filter and the x rows, then the state blocks of every row; a row with the pad slot or a slot
-// outside the cache skips its state load and all its stores. CHECK (a status word was given) adds
-// the report of slots outside the cache, which costs 0.35 us per call, so the unchecked variant
-// leaves it out.
+// thread (gridDim.y == ceil(B / R)), NB bytes of channels per thread, raw tap-major weights
+// widened at use, no runtime step loop (the general kernel's 90 registers halve the resident
+// threads). Every load is issued before any compute: the slot loads first, since each heads the
+// only dependent chain (slot -> state), then the filter and the x rows, then the state blocks of
+// every row; a row with the pad slot or a slot outside the cache skips its state load and all its
+// stores. CHECK (a status word was given) adds the report of slots outside the cache, which costs
+// 0.35 us per call, so the unchecked variant leaves it out.
 //
-// R = 2 with at least 7 resident CTAs per SM (72 registers) runs a batch of 256 rows in one wave
-// of CTAs, every thread keeping two rows' loads in flight; R = 1 (54 registers, 9 CTAs per SM)
-// needs 1.5 waves there. Measured on B200 at D = 8192, bf16, W = 4 (CUDA graphs, L2 flushed before
-// every call; R = 1 / R = 2, us): indexed B = 256, 1024-slot cache: 7.99 / 7.37 cold, 7.47 / 7.07
-// warm; direct B = 256: 7.78 / 7.27 cold. At B = 64 (one wave either way) R = 1 is faster: 3.48 /
-// 4.00 cold. Forms tried and not kept, all within 0.5 us of these: 16 channels per thread with
-// 32-byte accesses (32- to 256-thread CTAs), 4 or 8 rows per thread, the warp's state block moved
-// through shared memory with 512-byte coalesced accesses. The floor under them: an empty kernel on
-// the same grid costs 1.3-1.8 us, and a kernel that only loads the slot, then one 16-byte state
-// vector per thread, costs 5.7-6.3 us cold at B = 256 (two dependent DRAM round trips).
-template <typename T, int W, int SS, bool CHECK, int R>
+// Launch table (16-bit types): 4 channels per thread (8-byte vectors) and 2 rows per thread below
+// 128 rows, 4 rows per thread from 128 rows. Measured on B200 at D = 8192, bf16, W = 4, CUDA
+// graphs with a 256 MiB L2 flush before every call (cold) or back to back (warm), us, as
+// (R rows, NB bytes): direct B = 64: (1, 16) 3.84 / 3.19, (1, 8) 3.83 / 3.05, (2, 16) 4.06 / 3.24,
+// (2, 8) 3.60 / 2.72, (4, 8) 4.03 / 2.78; indexed B = 64 (1024-slot cache): (1, 16) 4.07 / 3.18,
+// (2, 8) 3.77 / 2.71; direct B = 256: (1, 16) 7.99 / 6.80, (2, 16) 7.30 / 6.99, (2, 8) 7.38 / 5.95,
+// (4, 8) 7.21 / 5.02; indexed B = 256: (2, 16) 7.71 / 7.26, (2, 8) 8.06 / 5.93, (4, 8) 8.15 / 5.41.
+// More rows per thread keep more independent loads in flight per thread; half-width vectors double
+// the threads. fp32 keeps one row of 16-byte vectors. The floor under all of them: an empty
+// kernel on the same grid costs 1.3-1.8 us, and a kernel that only loads the slot, then one
+// 16-byte state vector per thread, costs 5.7-6.3 us cold at B = 256 (two dependent DRAM round
+// trips). Forms tried and not kept: 16 channels per thread with 32-byte accesses (32- to
+// 256-thread CTAs), 8 rows per thread, the warp's state block moved through shared memory with
+// 512-byte coalesced accesses.
+template <typename T, int W, int SS, bool CHECK, int R, int NB>
 __global__ void __launch_bounds__(kUpdThreads, R == 1 ? 1 : 7) decode1_kernel(const UpdArgs a) {
-    constexpr int V = Vec<T>::V;
+    using RV = typename RawVec<NB>::type;
+    constexpr int V = NB / (int)sizeof(T);
     constexpr int K = W - 1;
     const int64_t nvec = a.D / V;
     const int64_t j = (int64_t)blockIdx.x * kUpdThreads + threadIdx.x;
@@ -189,24 +194,24 @@ __global__ void __launch_bounds__(kUpdThreads, R == 1 ? 1 : 7) decode1_kernel(co
         const int64_t b = (int64_t)blockIdx.y * R + r;
         slot[r] = b < a.B ? (a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b) : a.pad;
     }
-    uint4 wt[W], bt;
+    RV wt[W], bt;
     load_filter_raw<T, W>((const T*)a.w, W, 1, (const T*)a.bias, 1, c0, true, a.bias != nullptr,
                           wt, bt);
-    uint4 xr[R];
+    RV xr[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int64_t b = (int64_t)blockIdx.y * R + r;
-        if (b < a.B) xr[r] = ldg16((const T*)a.x + b * a.x_sb + c0);
+        if (b < a.B) xr[r] = ldg_raw<NB>((const T*)a.x + b * a.x_sb + c0);
     }
     bool live[R];
-    uint4 sr[R][SS];
+    RV sr[R][SS];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         live[r] = slot[r] != a.pad && slot[r] >= 0 && (int64_t)slot[r] < a.nslots;
         if (live[r]) {
             const T* sp = (const T*)a.state + (int64_t)slot[r] * a.s_slot + c0 * SS;
 #pragma unroll
-            for (int q = 0; q < SS; ++q) sr[r][q] = ld16(sp + q * V);
+            for (int q = 0; q < SS; ++q) sr[r][q] = ld_raw<NB>(sp + q * V);
         }
         if (CHECK && !live[r] && slot[r] != a.pad && j == 0) flag_status(a.status, CC1D_DEV_BAD_SLOT);
     }
@@ -215,34 +220,34 @@ __global__ void __launch_bounds__(kUpdThreads, R == 1 ? 1 : 7) decode1_kernel(co
     for (int r = 0; r < R; ++r) {
         if (!live[r]) continue;
         const int64_t b = (int64_t)blockIdx.y * R + r;
-        uint4 win[SS];
+        RV win[SS];
         block_to_time<T, SS>(sr[r], win);
         float acc[V];
-        unpack16<T>(bt, acc);
+        unpack_raw<T, NB>(bt, acc);
 #pragma unroll
         for (int k = 0; k < K; ++k) {
             float f[V], wk[V];
-            unpack16<T>(win[SS - K + k], f);
-            unpack16<T>(wt[k], wk);
+            unpack_raw<T, NB>(win[SS - K + k], f);
+            unpack_raw<T, NB>(wt[k], wk);
 #pragma unroll
             for (int e = 0; e < V; ++e) acc[e] = fmaf(f[e], wk[e], acc[e]);
         }
         {
             float f[V], wk[V];
-            unpack16<T>(xr[r], f);
-            unpack16<T>(wt[K], wk);
+            unpack_raw<T, NB>(xr[r], f);
+            unpack_raw<T, NB>(wt[K], wk);
 #pragma unroll
             for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), use_silu);
         }
-        st16((T*)a.out + b * a.o_sb + c0, pack16<T>(acc));
+        st_raw<NB>((T*)a.out + b * a.o_sb + c0, pack_raw<T, NB>(acc));
 #pragma unroll
         for (int s = 0; s + 1 < SS; ++s) win[s] = win[s + 1];
         win[SS - 1] = xr[r];
-        uint4 blk[SS];
+        RV blk[SS];
         time_to_block<T, SS>(win, blk);
         T* sp = (T*)a.state + (int64_t)slot[r] * a.s_slot + c0 * SS;
 #pragma unroll
-        for (int q = 0; q < SS; ++q) st16(sp + q * V, blk[q]);
+        for (int q = 0; q < SS; ++q) st_raw<NB>(sp + q * V, blk[q]);
     }
 }
 
@@ -326,16 +331,16 @@ cudaError_t launch_vec_inter(const UpdArgs& a, int imode, bool wvec, bool bvec,
 }
 
 // The lean single-step decode, R rows per thread, with or without the status report.
-template <typename T, int W, int K, int P, int R>
+template <typename T, int W, int K, int P, int R, int NB>
 cudaError_t launch_decode1(const UpdArgs& a, cudaStream_t stream) {
-    const int64_t nvec = a.D / Vec<T>::V;
+    const int64_t nvec = a.D / (NB / (int64_t)sizeof(T));
     dim3 grid((unsigned)ceil_div(nvec, kUpdThreads), (unsigned)ceil_div(a.B, (int64_t)R));
     if (a.status != nullptr) {
-        if (a.S == K) decode1_kernel<T, W, K, true, R><<<grid, kUpdThreads, 0, stream>>>(a);
-        else decode1_kernel<T, W, P, true, R><<<grid, kUpdThreads, 0, stream>>>(a);
+        if (a.S == K) decode1_kernel<T, W, K, true, R, NB><<<grid, kUpdThreads, 0, stream>>>(a);
+        else decode1_kernel<T, W, P, true, R, NB><<<grid, kUpdThreads, 0, stream>>>(a);
     } else {
-        if (a.S == K) decode1_kernel<T, W, K, false, R><<<grid, kUpdThreads, 0, stream>>>(a);
-        else decode1_kernel<T, W, P, false, R><<<grid, kUpdThreads, 0, stream>>>(a);
+        if (a.S == K) decode1_kernel<T, W, K, false, R, NB><<<grid, kUpdThreads, 0, stream>>>(a);
+        else decode1_kernel<T, W, P, false, R, NB><<<grid, kUpdThreads, 0, stream>>>(a);
     }
     return cudaGetLastError();
 }
@@ -369,9 +374,10 @@ cudaError_t run_update(const UpdArgs& a, cudaStream_t stream) {
     const bool lean = wvec && (a.bias == nullptr || bvec) && a.L == 1 && imode == kInterNone;
     if (xok && sok && iok && lean && (a.S == K || a.S == P) && a.B <= 65535) {
         if constexpr (sizeof(T) == 2 && W <= 4) {
-            if (a.B >= 128) return launch_decode1<T, W, K, P, 2>(a, stream);
+            if (a.B >= 128) return launch_decode1<T, W, K, P, 4, 8>(a, stream);
+            return launch_decode1<T, W, K, P, 2, 8>(a, stream);
         }
-        return launch_decode1<T, W, K, P, 1>(a, stream);
+        return launch_decode1<T, W, K, P, 1, 16>(a, stream);
     }
     if (xok && sok && iok && a.L >= 1 && a.L <= 16 && a.B <= 65535) {
         if (a.S == K) {

@@ -153,6 +153,96 @@ __global__ void __launch_bounds__(NT, MINB)
     }
 }
 
+// Staged form for 16-bit types up to W = 4 (as the plain channel-last prefill, fwd.cu): one CTA
+// per strip of S packed tokens and NT channel vectors, the strip and the W-1 rows before it landed
+// in shared memory by cp.async (stage_strip). The sequence search for the strip start runs while
+// the rows land. A strip that lies inside one sequence at least W-1 tokens after its start (all
+// but the few strips at sequence starts) walks its S rows with no per-row guard. Any other strip
+// takes the ownership rules of the register walk above: the thread whose strip holds a sequence's
+// first token reads its initial state, writes its final state and computes its first W-1 outputs
+// (reading the rows past the strip end from global memory), so no cache slot is read by one CTA
+// and written by another.
+template <typename T, int W, int S, int NT>
+__global__ void __launch_bounds__(NT)
+    varlen_staged_kernel(const VarArgs a, int64_t gx, bool wvec, bool bvec) {
+    constexpr int V = Vec<T>::V;
+    constexpr int K = W - 1;
+    constexpr int HALF = S / 2;
+    extern __shared__ uint4 stage[];
+    const int64_t blk = blockIdx.x;
+    const int64_t su = blk / gx;
+    const int64_t j = (blk - su * gx) * NT + threadIdx.x;
+    if (j >= a.D / V) return;
+    const int64_t c0 = j * V;
+    const int64_t t0 = su * S;
+    const int64_t t1 = min(t0 + S, a.T);
+    const int64_t n = t1 - t0;
+    const T* xb = (const T*)a.x + c0;
+    T* ob = (T*)a.out + c0;
+    uint4* col = stage + threadIdx.x;  // row t at col[(t - t0 + K) * NT]
+    if (n == S) stage_strip<T, K, S, NT, true>(col, xb, a.x_st, t0, n);
+    else stage_strip<T, K, S, NT, false>(col, xb, a.x_st, t0, n);
+    const int64_t s0 = seq_of(a, t0);
+    float w[W][V], bv[V];
+    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
+                      w, bv);
+    const bool use_silu = a.silu != 0;
+    prescale_filter<T, W>(w, bv, use_silu);
+    float h[K][V];
+    auto emit = [&](const uint4& r, int64_t t) {
+        float xv[V], o[V];
+        unpack16<T>(r, xv);
+        conv_step<T, W>(h, xv, w, bv, use_silu, o);
+        st16_stream(ob + t * a.o_st, pack16<T>(o));
+    };
+    auto staged = [&](int64_t t) -> const uint4& { return col[(t - t0 + K) * NT]; };
+    if (n == S && s0 >= 0 && s0 < a.nseq && qsl_at(a, s0) + K <= t0 && qsl_at(a, s0 + 1) >= t1) {
+        // The whole strip continues one sequence: history from the staged rows before it.
+        cp_async_wait<1>();
+#pragma unroll
+        for (int k = 0; k < K; ++k) unpack16<T>(col[k * NT], h[k]);
+#pragma unroll
+        for (int r = 0; r < HALF; ++r) emit(col[(K + r) * NT], t0 + r);
+        cp_async_wait<0>();
+#pragma unroll
+        for (int r = HALF; r < S; ++r) emit(col[(K + r) * NT], t0 + r);
+        return;
+    }
+    cp_async_wait<0>();
+    int64_t s = s0;
+    int64_t t = t0;
+    if (s < 0) {
+        t = min(t1, qsl_at(a, 0));
+        s = 0;
+    }
+    while (t < t1 && s < a.nseq) {
+        const int64_t bos = qsl_at(a, s);
+        const int64_t eos = max(qsl_at(a, s + 1), bos);
+        if (eos <= t) {
+            ++s;
+            continue;
+        }
+        const int64_t e = min(t1, eos);
+        int64_t ta, tb;
+        if (t == bos) {
+            owner_state<T, W, 16>(a, xb, c0, s, bos, eos, j == 0, h);
+            ta = bos;
+            tb = min(eos, max(e, bos + K));
+        } else {
+            ta = max(t, bos + K);
+            tb = e;
+            if (ta < tb) {
+#pragma unroll
+                for (int k = 0; k < K; ++k) unpack16<T>(staged(ta - K + k), h[k]);
+            }
+        }
+        for (int64_t u = ta; u < tb; ++u)
+            emit(u < t1 ? staged(u) : ldg16(xb + u * a.x_st), u);
+        t = e;
+        if (e == eos) ++s;
+    }
+}
+
 // ---------------------------------------------------------------------------------------------
 // Channel-first: x is contiguous (D, T), one packed stream per channel. The bulk pass is the
 // channel-first prefill of a (1, D, T) batch (launch_fwd): it computes every output as if each
@@ -372,6 +462,23 @@ cudaError_t run_varlen(const VarArgs& a, int dtype, cudaStream_t stream) {
                       (a.s_slot * e) % 16 == 0);
     const bool tm = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
                     host_aligned16(a.out) && (a.x_st * e) % 16 == 0 && (a.o_st * e) % 16 == 0;
+    if constexpr (sizeof(T) == 2 && W <= 4) {
+        // Staged 16-token strips, one per 64-thread CTA (varlen_staged_kernel). Measured on B200
+        // with the config-5 batch (bf16, 32 sequences, 40807 tokens x 8192 channels), staged vs
+        // the register walk below: W = 2: 201.4 vs 217.7 us; 3: 200.4 vs 223.6; 4: 211.8 vs 226.4.
+        // At W = 5 the staged kernel (128 registers, 6 CTAs per SM) lost: 6.0 vs 5.8 ns per token.
+        // A minimum of 9-12 resident CTAs in the launch bounds made every width slower (W = 4:
+        // 338.5 -> 397 us on a 66k-token batch) by capping registers below what the walk needs.
+        constexpr int S = 16, NT = 64;
+        const int64_t gx = ceil_div(a.D / V, (int64_t)NT);
+        const int64_t blocks = gx * ceil_div(a.T, (int64_t)S);
+        if (tm && sok && blocks <= 0x7fffffffLL) {
+            const size_t smem = (size_t)(S + K) * NT * 16;
+            varlen_staged_kernel<T, W, S, NT>
+                <<<(unsigned)blocks, NT, smem, stream>>>(a, gx, wvec, bvec);
+            return cudaGetLastError();
+        }
+    }
     if (tm && sok) {
         constexpr int NB = var_bytes<T, W>();
         constexpr int NT = var_threads<T, W>();

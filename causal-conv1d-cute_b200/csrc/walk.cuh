@@ -199,6 +199,30 @@ __device__ __forceinline__ void walk_strip_seq(const T* __restrict__ xb, int64_t
     for (; t < tb; ++t) emit(ldg16_stream(xb + t * x_st), __ldg(qb + t * q_st), t);
 }
 
+// Stage of a short strip in shared memory, for the staged kernels: a thread's 16-byte column of
+// the K rows before t0 and of the strip's rows t0.. t0+n-1 (n == S when FULL) lies at
+// col[r * NT], halo rows first. The halo rows at t >= 0 and the strip's first half are one
+// cp.async group, the second half another, so cp_async_wait<1>() makes the halo and the first half
+// readable while the rest lands. Halo rows at t < 0 are not touched: the caller fills them.
+template <typename T, int K, int S, int NT, bool FULL>
+__device__ __forceinline__ void stage_strip(uint4* col, const T* xb, int64_t x_st, int64_t t0,
+                                            int64_t n) {
+    constexpr int HALF = S / 2;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+        const int64_t t = t0 - K + k;
+        if (t >= 0) cp_async16(col + k * NT, xb + t * x_st);
+    }
+#pragma unroll
+    for (int i = 0; i < HALF; ++i)
+        if (FULL || i < n) cp_async16(col + (K + i) * NT, xb + (t0 + i) * x_st);
+    cp_async_commit();
+#pragma unroll
+    for (int i = HALF; i < S; ++i)
+        if (FULL || i < n) cp_async16(col + (K + i) * NT, xb + (t0 + i) * x_st);
+    cp_async_commit();
+}
+
 // Window of the W-1 rows before t0 (zeros before the sequence start).
 template <typename T, int W, int NB = 16>
 __device__ __forceinline__ void load_halo(const T* xb, int64_t x_st, int64_t t0,

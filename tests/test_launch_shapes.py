@@ -1,8 +1,12 @@
 """Shapes that reach each launch form of the token-row walks.
 
-The channel-last prefill and the token-major varlen kernels run either as fixed strips over
-several waves or as one wave of balanced shares, chosen on the host from the width, the sequence
-lengths and the GPU's resident-CTA count. These cases sit on both sides of that choice, with shares
+For 16-bit types up to W = 5 the channel-last prefill and the token-major varlen kernels run as
+staged 16-token strips (one per CTA, landed in shared memory); the cases below include partial last
+strips, partial channel blocks and, for varlen, sequence starts at every offset inside a strip,
+sequences shorter than W - 1 and heads that run past a strip end. Wider filters and fp32 take the
+register walks, either as fixed strips over several waves or as one wave of balanced shares, chosen
+on the host from the width, the sequence lengths and the GPU's resident-CTA count (the fp32 runs of
+the prefill cases reach those for W <= 5). These cases sit on both sides of that choice, with shares
 that cross batch and sequence boundaries and a partial last channel block, and check that the
 result is bit-identical to the scalar path (the same arithmetic in the same order, reached by
 viewing rows of a wider buffer that are not 16-byte aligned), and, for a small case, to the oracle.
@@ -45,19 +49,21 @@ def _unaligned_view(t, D):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("B,L,D,W", FWD_SHAPES)
-def test_prefill_launch_forms_match_scalar_path(B, L, D, W):
+def test_prefill_launch_forms_match_scalar_path(B, L, D, W, dtype):
     g = torch.Generator(device="cuda").manual_seed(B * 7919 + L * 31 + W)
-    x = torch.randn(B, L, D, device="cuda", dtype=torch.bfloat16, generator=g)
-    w = (torch.rand(D, W, device="cuda", generator=g) - 0.5).to(torch.bfloat16)
-    b = (torch.randn(D, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    x = torch.randn(B, L, D, device="cuda", generator=g).to(dtype)
+    w = (torch.rand(D, W, device="cuda", generator=g) - 0.5).to(dtype)
+    b = (torch.randn(D, device="cuda", generator=g) * 0.1).to(dtype)
     y = causal_conv1d_fn(x.transpose(1, 2), w, b, "silu")
     ys = causal_conv1d_fn(_unaligned_view(x, D).transpose(1, 2), w, b, "silu")
     torch.cuda.synchronize()
     assert torch.equal(y, ys)
     if B * L * D <= 1 << 20:
-        ref = oracle.fwd(to_np(x.transpose(1, 2)), to_np(w), to_np(b), True, "bf16")
-        assert_close(y, ref, torch.bfloat16)
+        name = "bf16" if dtype == torch.bfloat16 else "f32"
+        ref = oracle.fwd(to_np(x.transpose(1, 2)), to_np(w), to_np(b), True, name)
+        assert_close(y, ref, dtype)
 
 
 # (lengths, D, W): many short sequences (strips at W = 2), lognormal lengths with balanced shares
@@ -74,6 +80,12 @@ VARLEN_CASES = [
     ([1, 2, 3, 0, 9, 1, 700, 2, 5], 1024, 8),
     (_lengths(4, 20, 6.0), 1000, 5),
     (_lengths(5, 12, 6.5), 776, 6),
+    # staged strips: starts at every offset of a 16-token strip, sequences shorter than W - 1,
+    # heads past a strip end, a partial last strip (T = 79) and a partial channel block (D = 520)
+    ([1, 2, 3, 13, 15, 16, 17, 1, 31, 2, 3, 45, 14, 18, 7, 4, 5, 6, 8, 9, 10, 11, 12], 512, 4),
+    ([5, 11, 16, 1, 1, 1, 40, 3, 29, 2, 14, 0, 17], 520, 5),
+    ([15, 17, 33, 14], 256, 3),
+    (_lengths(6, 60, 2.5), 1024, 2),
 ]
 
 

@@ -62,7 +62,7 @@ def test_ring_decode_matches_oracle(seed):
     torch.manual_seed(seed)
     D = random.choice([64, 1024, 2048, 10240, 8192, 100])
     W = random.choice([2, 3, 4, 4, 4, 5, 8])
-    B = random.choice([1, 2, 5, 48])
+    B = random.choice([1, 2, 5, 48, 130, 131])  # 2 rows per thread below 128, 4 from 128
     dtype = random.choice([torch.bfloat16, torch.bfloat16, torch.float16, torch.float32])
     act = random.choice([None, "silu"])
     indexed = random.random() < 0.5

@@ -13,7 +13,7 @@ from causal_conv1d_cute.api import padded_width
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B", [1, 3, 64])
+@pytest.mark.parametrize("B", [1, 3, 64, 131])
 @pytest.mark.parametrize("act", [None, "silu"])
 @pytest.mark.parametrize("bias", [False, True])
 @pytest.mark.parametrize("W", [2, 3, 4, 5, 6, 7, 8])
@@ -49,7 +49,7 @@ def test_against_oracle(dtype, W):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B", [1, 8, 256])
+@pytest.mark.parametrize("B", [1, 8, 131, 256])
 @pytest.mark.parametrize(
     "D,W,bias,act", [(1536, 7, True, None), (2048, 3, False, None), (2048, 4, False, "silu"),
                      (256, 2, True, "silu")]
