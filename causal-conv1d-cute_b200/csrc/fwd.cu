@@ -1,8 +1,8 @@
 // Prefill over dense batched sequences (replaces causal_conv1d_cute/fwd.py).
 //
 // Kernels, chosen by layout and width in run_fwd:
-//   fwd_channel_last_staged  (B, L, D) storage, 16-bit types, W <= 5: one CTA per strip of 16
-//                      tokens of one batch row and 64 16-byte channel vectors; each thread lands
+//   fwd_channel_last_staged  (B, L, D) storage, 16-bit types: one CTA per strip of 16 (32 at
+//                      W = 8) tokens of one batch row and 64 16-byte channel vectors; each thread lands
 //                      its column of the strip (and the W-1 rows before it) in shared memory with
 //                      cp.async and walks it there. Many short-lived CTAs, several waves.
 //   fwd_channel_last   (B, L, D) storage otherwise (x_sd == 1): every thread owns one 16-byte (or
@@ -89,15 +89,38 @@ __global__ void __launch_bounds__(NT, MINB)
     }
 }
 
-// One strip of n rows (n == S when FULL): copies, filter, then the walk from shared memory. The
-// full-strip form has no per-row guard, so the window shift of every row is a static register
-// renaming; a guard on each row turns it into a select per window register (the W = 4 kernel took
-// 243 instead of 164 us at the config-2 shape that way), so only a batch row's last strip, when
-// L is not a multiple of S, takes the guarded form.
-template <typename T, int W, int S, int NT, bool FULL>
+// The staged walk (one strip of 16 tokens, 32 at W = 8, per 64-thread CTA, rows landed in shared
+// memory by cp.async, channel pairs by packed FMAs) serves 16-bit types at every width. Measured on
+// B200 at the config-2 shape (8 x 4096 x 8192 bf16, one launch at a time; staged vs the register
+// walk below, us): W = 2: 163.7 vs 174.1; 3: 163.9 vs 176.6; 4: 162.3 vs 184.1; 5: 161.8 vs 185.5;
+// 6: 162.0 vs 185.5 (175.2 with the default budget of 130 registers, 7 CTAs per SM; a separate
+// kernel asks for 8); 7: 179.7 vs 186.6; 8: 189.2 vs 198.7. The library's copy of the same bytes
+// takes 160-161 us. Longer strips
+// lost at W <= 7 (W = 4: 32 tokens 175.7 us, 64: 256.5 us: fewer CTAs fit and each lives longer)
+// and 16 tokens lost at W = 8 (222-248 us: the 7 halo rows are a larger share of each strip); so
+// did the same strips walked from registers (16 tokens, all loads up front: 210 us at W = 4,
+// spilling), one-thread bulk copies of whole 1 KB row segments on an mbarrier (164.8 us, no gain),
+// scalar FMAs (W = 7: 211 us, W = 8: 242 us), SiLU tested at run time (W = 5: 183.6 us), run-time
+// weight and bias layout flags (W = 8: 196 -> 190 us when constant) and a minimum of 9-12
+// resident CTAs in the launch bounds at W <= 5 (it spills). fp32 keeps the register walk.
+constexpr int kStageThreads = 64;
+template <typename T, int W>
+constexpr bool staged_prefill() {
+    return sizeof(T) == 2;
+}
+template <int W>
+constexpr int stage_rows() {
+    return W == 8 ? 32 : 16;
+}
+
+// One strip of n rows (n == S when FULL): copies, filter, then the walk from shared memory in
+// channel pairs (conv_step_x2). The full-strip form has no per-row guard, so the window shift of
+// every row is a static register renaming; a guard on each row turns it into a select per window
+// register (the W = 4 kernel took 243 instead of 164 us at the config-2 shape that way), so only a
+// batch row's last strip, when L is not a multiple of S, takes the guarded form.
+template <typename T, int W, int S, int NT, bool SILU, bool FULL>
 __device__ __forceinline__ void staged_strip(const FwdArgs& a, uint4* col, const T* xb, T* ob,
-                                             int64_t t0, int64_t n, int64_t c0, bool wvec,
-                                             bool bvec) {
+                                             int64_t t0, int64_t n, int64_t c0) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     constexpr int HALF = S / 2;
@@ -105,21 +128,22 @@ __device__ __forceinline__ void staged_strip(const FwdArgs& a, uint4* col, const
 #pragma unroll
     for (int k = 0; k < K; ++k)
         if (t0 - K + k < 0) col[k * NT] = make_uint4(0u, 0u, 0u, 0u);
-    float w[W][V], bv[V];
-    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
-                      w, bv);
-    const bool use_silu = a.silu != 0;
-    prescale_filter<T, W>(w, bv, use_silu);
-    float h[K][V];
+    Pairs w2[W], b2;
+    {
+        float w[W][V], bv[V];
+        load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, true,
+                          true, w, bv);
+        prescale_filter<T, W>(w, bv, SILU);
+        filter_pairs<W>(w, bv, w2, b2);
+    }
+    Pairs h[K];
     auto row = [&](int r) {
-        float xv[V], o[V];
-        unpack16<T>(col[(K + r) * NT], xv);
-        conv_step<T, W>(h, xv, w, bv, use_silu, o);
-        st16_stream(ob + (t0 + r) * a.o_sl, pack16<T>(o));
+        const Pairs o = conv_step_x2<W, SILU>(h, to_pairs<T>(col[(K + r) * NT]), w2, b2);
+        st16_stream(ob + (t0 + r) * a.o_sl, from_pairs<T>(o));
     };
     cp_async_wait<1>();
 #pragma unroll
-    for (int k = 0; k < K; ++k) unpack16<T>(col[k * NT], h[k]);
+    for (int k = 0; k < K; ++k) h[k] = to_pairs<T>(col[k * NT]);
     if (FULL) {
 #pragma unroll
         for (int r = 0; r < HALF; ++r) row(r);
@@ -140,11 +164,18 @@ __device__ __forceinline__ void staged_strip(const FwdArgs& a, uint4* col, const
 // lands) and walks the rows from shared memory. No thread reads another's column, so there is no
 // barrier. The grid runs many short-lived CTAs back to back, which keeps the bytes requested from
 // DRAM at any moment within a narrow window of consecutive rows, as a copy does; the halo rows
-// were just read by the neighbouring strip's CTA and come from L2.
-template <typename T, int W, int S, int NT>
-__global__ void __launch_bounds__(NT)
-    fwd_channel_last_staged_kernel(const FwdArgs a, int64_t nstrips, int64_t gx, bool wvec,
-                                   bool bvec) {
+// were just read by the neighbouring strip's CTA and come from L2. 16-bit types only (the pair
+// arithmetic takes 8 channels per 16-byte vector); the weights are the contiguous (dim, W) tensor
+// and the bias, if any, is contiguous (the host sends other layouts to the register walk).
+//
+// One launch covers strips strip0 .. strip0 + nstrips - 1 of every batch row. FULL launches cover
+// the whole strips; a second, guarded launch (FULL false, nstrips 1) covers each row's last strip
+// when L is not a multiple of S. The two forms are separate kernels because the guarded form's
+// registers would otherwise be the whole kernel's (W = 8: 250 instead of 166 registers, 210 instead
+// of 196 us at the config-2 shape).
+template <typename T, int W, int S, int NT, bool SILU, bool FULL>
+__device__ __forceinline__ void staged_cta(const FwdArgs& a, int64_t nstrips, int64_t gx,
+                                           int64_t strip0) {
     constexpr int V = Vec<T>::V;
     extern __shared__ uint4 stage[];
     const int64_t blk = blockIdx.x;
@@ -152,14 +183,50 @@ __global__ void __launch_bounds__(NT)
     const int64_t j = (blk - su * gx) * NT + threadIdx.x;
     if (j >= a.D / V) return;
     const int64_t b = su / nstrips;
-    const int64_t t0 = (su - b * nstrips) * S;
-    const int64_t n = min((int64_t)S, a.L - t0);
+    const int64_t t0 = (strip0 + su - b * nstrips) * S;
+    const int64_t n = FULL ? S : a.L - t0;
     const int64_t c0 = j * V;
     const T* xb = (const T*)a.x + b * a.x_sb + c0;
     T* ob = (T*)a.out + b * a.o_sb + c0;
     uint4* col = stage + threadIdx.x;  // row r of the stage (halo rows first) at col[r * NT]
-    if (n == S) staged_strip<T, W, S, NT, true>(a, col, xb, ob, t0, n, c0, wvec, bvec);
-    else staged_strip<T, W, S, NT, false>(a, col, xb, ob, t0, n, c0, wvec, bvec);
+    staged_strip<T, W, S, NT, SILU, FULL>(a, col, xb, ob, t0, n, c0);
+}
+
+// The launch bounds name no minimum of resident CTAs: with an explicit minimum of 1 the compiler
+// spends registers freely (W = 4: 194 instead of 98, W = 2: 174 instead of 60) and the kernel
+// fits half as many CTAs per SM (W = 4: 198 instead of 163 us at the config-2 shape).
+template <typename T, int W, int S, int NT, bool SILU, bool FULL>
+__global__ void __launch_bounds__(NT)
+    fwd_channel_last_staged_kernel(const FwdArgs a, int64_t nstrips, int64_t gx, int64_t strip0) {
+    staged_cta<T, W, S, NT, SILU, FULL>(a, nstrips, gx, strip0);
+}
+
+// W = 6 with SiLU, whole strips: the default budget (130 registers) leaves 7 CTAs per SM; a
+// minimum of 8 fits it in 128 registers without spilling.
+template <typename T, int S, int NT>
+__global__ void __launch_bounds__(NT, 8)
+    fwd_channel_last_staged_w6_kernel(const FwdArgs a, int64_t nstrips, int64_t gx) {
+    staged_cta<T, 6, S, NT, true, true>(a, nstrips, gx, 0);
+}
+
+// The full-strip launch and, when L is not a multiple of S, the last-strip launch.
+template <typename T, int W, int S, bool SILU>
+cudaError_t launch_staged(const FwdArgs& a, int64_t gx, cudaStream_t stream) {
+    const size_t smem = (size_t)(S + W - 1) * kStageThreads * 16;
+    const int64_t full = a.L / S;
+    if (full > 0) {
+        if constexpr (W == 6 && SILU)
+            fwd_channel_last_staged_w6_kernel<T, S, kStageThreads>
+                <<<(unsigned)(gx * a.B * full), kStageThreads, smem, stream>>>(a, full, gx);
+        else
+            fwd_channel_last_staged_kernel<T, W, S, kStageThreads, SILU, true>
+                <<<(unsigned)(gx * a.B * full), kStageThreads, smem, stream>>>(a, full, gx, 0);
+    }
+    if (a.L % S != 0) {
+        fwd_channel_last_staged_kernel<T, W, S, kStageThreads, SILU, false>
+            <<<(unsigned)(gx * a.B), kStageThreads, smem, stream>>>(a, 1, gx, full);
+    }
+    return cudaGetLastError();
 }
 
 // Flat-stream kernel for contiguous (B, D, L) with L >= EPT. Element f sits at row f / L (channel
@@ -412,25 +479,6 @@ constexpr int share_min_ctas() {
     return W >= 5 ? 1 : 0;
 }
 
-// The staged walk (one 16-token strip per 64-thread CTA, rows landed in shared memory by
-// cp.async) serves 16-bit types up to W = 5. Measured on B200 at the config-2 shape (8 x 4096 x
-// 8192 bf16, one launch at a time; staged vs the register walk above, us): W = 2: 161.7 vs 174.1;
-// 3: 166.3 vs 176.6; 4: 165.4 vs 184.1; 5: 183.6 vs 185.5. The library's copy of the same bytes
-// takes 160-161 us. A minimum of 10-12 resident CTAs in the launch bounds gained nothing at
-// W <= 4 and made W = 5 slower (242 us), since it caps registers below what the walk needs. Longer strips lost (W = 4: 32 tokens 175.7 us, 64: 256.5 us: fewer CTAs fit and
-// each lives longer), as did the same strips walked from registers (16 tokens, all loads up front:
-// 210 us at W = 4, spilling) and with one-thread bulk copies of whole 1 KB row segments on an
-// mbarrier (164.8 us, no gain). From W = 6 the filter and window of a 16-byte vector leave too
-// few CTAs per SM and the 8-byte form re-reads a relatively longer halo (W = 8: 226-237 us
-// against 199 us for the register walk), so wide filters and fp32 keep the register walk.
-constexpr int kStageRows = 16;
-constexpr int kStageThreads = 64;
-template <typename T, int W>
-constexpr bool staged_prefill() {
-    return sizeof(T) == 2 && W <= 5;
-}
-
-
 // Elements per lane of the flat-stream kernel. 32 (four 16-byte vectors, 123-128 registers, two
 // CTAs per SM) halves the warp-shuffle halo and loop overhead per element against 16 (64-88
 // registers, three CTAs per SM). Measured on B200, bf16, 8192 channels, 16 -> 32 elements (us):
@@ -487,16 +535,12 @@ cudaError_t run_fwd(const FwdArgs& a, cudaStream_t stream) {
     if (cl) {
         const int64_t nvec = a.D / V;
         if constexpr (staged_prefill<T, W>()) {
+            constexpr int S = stage_rows<W>();
             const int64_t sgx = ceil_div(nvec, (int64_t)kStageThreads);
-            const int64_t nstrips = ceil_div(a.L, (int64_t)kStageRows);
-            const int64_t blocks = sgx * a.B * nstrips;
-            if (blocks <= 0x7fffffffLL) {
-                const size_t smem = (size_t)(kStageRows + W - 1) * kStageThreads * 16;
-                fwd_channel_last_staged_kernel<T, W, kStageRows, kStageThreads>
-                    <<<(unsigned)blocks, kStageThreads, smem, stream>>>(a, nstrips, sgx, wvec,
-                                                                        bvec);
-                return cudaGetLastError();
-            }
+            const int64_t blocks = sgx * a.B * ceil_div(a.L, (int64_t)S);
+            if (wvec && (a.bias == nullptr || bvec) && blocks <= 0x7fffffffLL)
+                return a.silu ? launch_staged<T, W, S, true>(a, sgx, stream)
+                              : launch_staged<T, W, S, false>(a, sgx, stream);
         }
         const int64_t gx = ceil_div(nvec, (int64_t)kClThreads);
         constexpr int SB = share_bytes<T, W>();

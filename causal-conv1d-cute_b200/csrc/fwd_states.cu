@@ -11,8 +11,8 @@
 // (zeros in place of init without initial states), copied bit for bit from the inputs.
 //
 // Kernels:
-//   fwd_states_staged_kernel  channel-last x / out, 16-bit types, W <= 5, no sequence ids: the
-//                           staged 16-token strips of the plain prefill (one per CTA, landed in
+//   fwd_states_staged_kernel  channel-last x / out, 16-bit types, no sequence ids: the
+//                           staged strips of the plain prefill (one per CTA, landed in
 //                           shared memory), initial states in the halo of a row's first strip.
 //   fwd_states_vec_kernel   channel-last x / out otherwise (16-byte channel vectors, the walk and
 //                           grid of the plain channel-last register walk): a thread walks a share
@@ -133,16 +133,15 @@ __global__ void __launch_bounds__(kStThreads)
     }
 }
 
-// Staged form for 16-bit types up to W = 5 (the launch table of the plain prefill, fwd.cu): one
+// Staged form for 16-bit types (the launch table of the plain prefill, fwd.cu): one
 // CTA per strip of S tokens of one batch row and NT channel vectors, the strip landed in shared
 // memory by cp.async (stage_strip). History before token 0 is the initial states (zeros without
 // them), written into the stage's halo rows; the strip that ends a row writes that row's final
 // states. Calls with sequence ids keep the register walk (see the launch table). FULL: a whole
 // strip of S rows (no per-row guard, see the plain staged kernel).
-template <typename T, int W, int S, int NT, bool FULL>
+template <typename T, int W, int S, int NT, bool SILU, bool FULL>
 __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, int64_t b,
-                                             int64_t t0, int64_t n, int64_t c0, bool wvec,
-                                             bool bvec) {
+                                             int64_t t0, int64_t n, int64_t c0) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     constexpr int HALF = S / 2;
@@ -163,22 +162,23 @@ __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, 
             col[k * NT] = v;
         }
     }
-    float w[W][V], bv[V];
-    load_filter<T, W>((const T*)f.w, f.w_sd, f.w_sk, (const T*)f.bias, f.bias_s, c0, wvec, bvec,
-                      w, bv);
-    const bool use_silu = f.silu != 0;
-    prescale_filter<T, W>(w, bv, use_silu);
+    Pairs w2[W], b2;
+    {
+        float w[W][V], bv[V];
+        load_filter<T, W>((const T*)f.w, f.w_sd, f.w_sk, (const T*)f.bias, f.bias_s, c0, true,
+                          true, w, bv);
+        prescale_filter<T, W>(w, bv, SILU);
+        filter_pairs<W>(w, bv, w2, b2);
+    }
     T* ob = (T*)f.out + b * f.o_sb + c0;
-    float h[K][V];
+    Pairs h[K];
     auto row = [&](int r) {
-        float xv[V], o[V];
-        unpack16<T>(col[(K + r) * NT], xv);
-        conv_step<T, W>(h, xv, w, bv, use_silu, o);
-        st16_stream(ob + (t0 + r) * f.o_sl, pack16<T>(o));
+        const Pairs o = conv_step_x2<W, SILU>(h, to_pairs<T>(col[(K + r) * NT]), w2, b2);
+        st16_stream(ob + (t0 + r) * f.o_sl, from_pairs<T>(o));
     };
     cp_async_wait<1>();
 #pragma unroll
-    for (int k = 0; k < K; ++k) unpack16<T>(col[k * NT], h[k]);
+    for (int k = 0; k < K; ++k) h[k] = to_pairs<T>(col[k * NT]);
     if (FULL) {
 #pragma unroll
         for (int r = 0; r < HALF; ++r) row(r);
@@ -187,17 +187,16 @@ __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, 
         for (int r = HALF; r < S; ++r) row(r);
     } else {
         cp_async_wait<0>();
-#pragma unroll
-        for (int r = 0; r < S; ++r)
-            if (r < n) row(r);
+        for (int r = 0; r < n; ++r) row(r);
     }
     if (a.fin != nullptr && t0 + n == f.L) states_final<T, W>(a, b, c0, V);
 }
 
-template <typename T, int W, int S, int NT>
+// Strips strip0 .. strip0 + nstrips - 1 of every batch row: whole strips (FULL) in one launch, each
+// row's last partial strip in a second one, as the plain staged prefill (fwd.cu).
+template <typename T, int W, int S, int NT, bool SILU, bool FULL>
 __global__ void __launch_bounds__(NT)
-    fwd_states_staged_kernel(const FwdStateArgs a, int64_t nstrips, int64_t gx, bool wvec,
-                             bool bvec) {
+    fwd_states_staged_kernel(const FwdStateArgs a, int64_t nstrips, int64_t gx, int64_t strip0) {
     constexpr int V = Vec<T>::V;
     extern __shared__ uint4 stage[];
     const int64_t blk = blockIdx.x;
@@ -205,11 +204,24 @@ __global__ void __launch_bounds__(NT)
     const int64_t j = (blk - su * gx) * NT + threadIdx.x;
     if (j >= a.f.D / V) return;
     const int64_t b = su / nstrips;
-    const int64_t t0 = (su - b * nstrips) * S;
-    const int64_t n = min((int64_t)S, a.f.L - t0);
-    uint4* col = stage + threadIdx.x;
-    if (n == S) states_strip<T, W, S, NT, true>(a, col, b, t0, n, j * V, wvec, bvec);
-    else states_strip<T, W, S, NT, false>(a, col, b, t0, n, j * V, wvec, bvec);
+    const int64_t t0 = (strip0 + su - b * nstrips) * S;
+    const int64_t n = FULL ? S : a.f.L - t0;
+    states_strip<T, W, S, NT, SILU, FULL>(a, stage + threadIdx.x, b, t0, n, j * V);
+}
+
+template <typename T, int W, int S, int NT, bool SILU>
+cudaError_t launch_states_staged(const FwdStateArgs& a, int64_t gx, cudaStream_t stream) {
+    const size_t smem = (size_t)(S + W - 1) * NT * 16;
+    const int64_t full = a.f.L / S;
+    if (full > 0) {
+        fwd_states_staged_kernel<T, W, S, NT, SILU, true>
+            <<<(unsigned)(gx * a.f.B * full), NT, smem, stream>>>(a, full, gx, 0);
+    }
+    if (a.f.L % S != 0) {
+        fwd_states_staged_kernel<T, W, S, NT, SILU, false>
+            <<<(unsigned)(gx * a.f.B), NT, smem, stream>>>(a, 1, gx, full);
+    }
+    return cudaGetLastError();
 }
 
 // Any strides: thread = (row, channel, strip of kStStrip tokens).
@@ -289,22 +301,21 @@ cudaError_t run_fwd_states(const FwdStateArgs& a, cudaStream_t stream) {
     const bool cl = f.x_sd == 1 && f.o_sd == 1 && f.D % V == 0 && host_aligned16(f.x) &&
                     host_aligned16(f.out) && (f.x_sl * e) % 16 == 0 && (f.o_sl * e) % 16 == 0 &&
                     (f.x_sb * e) % 16 == 0 && (f.o_sb * e) % 16 == 0;
-    if constexpr (sizeof(T) == 2 && W <= 5) {
-        // Staged 16-token strips, one per 64-thread CTA, as the plain channel-last prefill.
+    if constexpr (sizeof(T) == 2) {
+        // Staged strips of 16 tokens (32 at W = 8), one per 64-thread CTA, as the plain
+        // channel-last prefill (channel pairs, compile-time SiLU).
         // Measured on B200 at the config-2 shape (bf16, W = 4), staged vs the balanced register
-        // walk below: initial + final states 172.5 vs 182.9 us; with sequence ids 183.4 vs
-        // 181.3 us (the per-row ids and masked taps cost more than staging saves), so calls with
-        // sequence ids keep the register walk.
-        constexpr int S = 16, NT = 64;
+        // walk below: initial + final states 163.3 vs 182.9 us (172.5 with scalar FMAs and a
+        // run-time SiLU); with sequence ids a staged form with scalar FMAs took 183.4 vs 181.3 us
+        // (the per-row ids and masked taps cost more than staging saves), so calls with sequence
+        // ids keep the register walk.
+        constexpr int S = W == 8 ? 32 : 16, NT = 64;
         const int64_t gx = ceil_div(f.D / V, (int64_t)NT);
-        const int64_t strips = ceil_div(f.L, (int64_t)S);
-        const int64_t blocks = gx * f.B * strips;
-        if (cl && f.L > 0 && a.seq == nullptr && blocks <= 0x7fffffffLL) {
-            const size_t smem = (size_t)(S + W - 1) * NT * 16;
-            fwd_states_staged_kernel<T, W, S, NT>
-                <<<(unsigned)blocks, NT, smem, stream>>>(a, strips, gx, wvec, bvec);
-            return cudaGetLastError();
-        }
+        const int64_t blocks = gx * f.B * ceil_div(f.L, (int64_t)S);
+        if (cl && f.L > 0 && a.seq == nullptr && wvec && (f.bias == nullptr || bvec) &&
+            blocks <= 0x7fffffffLL)
+            return f.silu ? launch_states_staged<T, W, S, NT, true>(a, gx, stream)
+                          : launch_states_staged<T, W, S, NT, false>(a, gx, stream);
     }
     if (cl) {
         // Launch table as for the plain channel-last prefill (fwd.cu): many ~128-row shares,

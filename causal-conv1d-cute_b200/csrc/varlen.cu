@@ -153,18 +153,20 @@ __global__ void __launch_bounds__(NT, MINB)
     }
 }
 
-// Staged form for 16-bit types up to W = 4 (as the plain channel-last prefill, fwd.cu): one CTA
+// Staged form for 16-bit types (as the plain channel-last prefill, fwd.cu): one CTA
 // per strip of S packed tokens and NT channel vectors, the strip and the W-1 rows before it landed
-// in shared memory by cp.async (stage_strip). The sequence search for the strip start runs while
+// in shared memory by cp.async (stage_strip), walked in channel pairs (conv_step_x2); contiguous
+// weights and bias (the host sends other layouts to the register walk). The sequence search for
+// the strip start runs while
 // the rows land. A strip that lies inside one sequence at least W-1 tokens after its start (all
 // but the few strips at sequence starts) walks its S rows with no per-row guard. Any other strip
 // takes the ownership rules of the register walk above: the thread whose strip holds a sequence's
 // first token reads its initial state, writes its final state and computes its first W-1 outputs
 // (reading the rows past the strip end from global memory), so no cache slot is read by one CTA
 // and written by another.
-template <typename T, int W, int S, int NT>
+template <typename T, int W, int S, int NT, bool SILU>
 __global__ void __launch_bounds__(NT)
-    varlen_staged_kernel(const VarArgs a, int64_t gx, bool wvec, bool bvec) {
+    varlen_staged_kernel(const VarArgs a, int64_t gx) {
     constexpr int V = Vec<T>::V;
     constexpr int K = W - 1;
     constexpr int HALF = S / 2;
@@ -183,24 +185,25 @@ __global__ void __launch_bounds__(NT)
     if (n == S) stage_strip<T, K, S, NT, true>(col, xb, a.x_st, t0, n);
     else stage_strip<T, K, S, NT, false>(col, xb, a.x_st, t0, n);
     const int64_t s0 = seq_of(a, t0);
-    float w[W][V], bv[V];
-    load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec, bvec,
-                      w, bv);
-    const bool use_silu = a.silu != 0;
-    prescale_filter<T, W>(w, bv, use_silu);
-    float h[K][V];
+    Pairs w2[W], b2;
+    {
+        float w[W][V], bv[V];
+        load_filter<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, true,
+                          true, w, bv);
+        prescale_filter<T, W>(w, bv, SILU);
+        filter_pairs<W>(w, bv, w2, b2);
+    }
+    Pairs h[K];
     auto emit = [&](const uint4& r, int64_t t) {
-        float xv[V], o[V];
-        unpack16<T>(r, xv);
-        conv_step<T, W>(h, xv, w, bv, use_silu, o);
-        st16_stream(ob + t * a.o_st, pack16<T>(o));
+        const Pairs o = conv_step_x2<W, SILU>(h, to_pairs<T>(r), w2, b2);
+        st16_stream(ob + t * a.o_st, from_pairs<T>(o));
     };
     auto staged = [&](int64_t t) -> const uint4& { return col[(t - t0 + K) * NT]; };
     if (n == S && s0 >= 0 && s0 < a.nseq && qsl_at(a, s0) + K <= t0 && qsl_at(a, s0 + 1) >= t1) {
         // The whole strip continues one sequence: history from the staged rows before it.
         cp_async_wait<1>();
 #pragma unroll
-        for (int k = 0; k < K; ++k) unpack16<T>(col[k * NT], h[k]);
+        for (int k = 0; k < K; ++k) h[k] = to_pairs<T>(col[k * NT]);
 #pragma unroll
         for (int r = 0; r < HALF; ++r) emit(col[(K + r) * NT], t0 + r);
         cp_async_wait<0>();
@@ -225,7 +228,12 @@ __global__ void __launch_bounds__(NT)
         const int64_t e = min(t1, eos);
         int64_t ta, tb;
         if (t == bos) {
-            owner_state<T, W, 16>(a, xb, c0, s, bos, eos, j == 0, h);
+            float hf[K][V];
+            owner_state<T, W, 16>(a, xb, c0, s, bos, eos, j == 0, hf);
+#pragma unroll
+            for (int k = 0; k < K; ++k)
+#pragma unroll
+                for (int q = 0; q < kPairs; ++q) h[k].p[q] = make_float2(hf[k][2 * q], hf[k][2 * q + 1]);
             ta = bos;
             tb = min(eos, max(e, bos + K));
         } else {
@@ -233,7 +241,7 @@ __global__ void __launch_bounds__(NT)
             tb = e;
             if (ta < tb) {
 #pragma unroll
-                for (int k = 0; k < K; ++k) unpack16<T>(staged(ta - K + k), h[k]);
+                for (int k = 0; k < K; ++k) h[k] = to_pairs<T>(staged(ta - K + k));
             }
         }
         for (int64_t u = ta; u < tb; ++u)
@@ -462,20 +470,23 @@ cudaError_t run_varlen(const VarArgs& a, int dtype, cudaStream_t stream) {
                       (a.s_slot * e) % 16 == 0);
     const bool tm = a.x_sd == 1 && a.o_sd == 1 && a.D % V == 0 && host_aligned16(a.x) &&
                     host_aligned16(a.out) && (a.x_st * e) % 16 == 0 && (a.o_st * e) % 16 == 0;
-    if constexpr (sizeof(T) == 2 && W <= 4) {
-        // Staged 16-token strips, one per 64-thread CTA (varlen_staged_kernel). Measured on B200
-        // with the config-5 batch (bf16, 32 sequences, 40807 tokens x 8192 channels), staged vs
-        // the register walk below: W = 2: 201.4 vs 217.7 us; 3: 200.4 vs 223.6; 4: 211.8 vs 226.4.
-        // At W = 5 the staged kernel (128 registers, 6 CTAs per SM) lost: 6.0 vs 5.8 ns per token.
-        // A minimum of 9-12 resident CTAs in the launch bounds made every width slower (W = 4:
-        // 338.5 -> 397 us on a 66k-token batch) by capping registers below what the walk needs.
+    if constexpr (sizeof(T) == 2 && W <= 7) {
+        // Staged strips of 16 tokens, one per 64-thread CTA (varlen_staged_kernel), as the plain
+        // channel-last prefill, up to W = 7. Measured on B200 with the config-5 batch (bf16, 32
+        // sequences, 40807 tokens x 8192 channels), staged (channel pairs, compile-time SiLU) vs
+        // the register walk below, us: W = 2: 203.1 vs 217.7; 3: 201.8 vs 223.6; 4: 202.3 vs
+        // 226.4; 5: 213.9 vs 235.7; 6: 224.0 vs 238.7; 7: 236.7 vs 239.1; 8 (32-token strips):
+        // 243.8-248.7 vs 240.7, so W = 8 keeps the register walk. A minimum of 9-12 resident CTAs
+        // in the launch bounds made every width slower (W = 4: 338.5 -> 397 us on a 66k-token
+        // batch) by capping registers.
         constexpr int S = 16, NT = 64;
         const int64_t gx = ceil_div(a.D / V, (int64_t)NT);
         const int64_t blocks = gx * ceil_div(a.T, (int64_t)S);
-        if (tm && sok && blocks <= 0x7fffffffLL) {
+        if (tm && sok && wvec && (a.bias == nullptr || bvec) && blocks <= 0x7fffffffLL) {
             const size_t smem = (size_t)(S + K) * NT * 16;
-            varlen_staged_kernel<T, W, S, NT>
-                <<<(unsigned)blocks, NT, smem, stream>>>(a, gx, wvec, bvec);
+            auto kern = a.silu ? varlen_staged_kernel<T, W, S, NT, true>
+                               : varlen_staged_kernel<T, W, S, NT, false>;
+            kern<<<(unsigned)blocks, NT, smem, stream>>>(a, gx);
             return cudaGetLastError();
         }
     }

@@ -199,6 +199,72 @@ __device__ __forceinline__ void walk_strip_seq(const T* __restrict__ xb, int64_t
     for (; t < tb; ++t) emit(ldg16_stream(xb + t * x_st), __ldg(qb + t * q_st), t);
 }
 
+// Packed form of conv_step for the staged kernels: a 16-byte vector of a 16-bit type (8
+// channels) as 4 channel pairs, every tap one fp32x2 fused multiply-add (__ffma2_rn, which rounds
+// each lane as fmaf does, so the bits equal conv_step's) and SILU fixed at compile time. Against
+// 8 scalar FMAs per tap this halves the arithmetic instructions, which bound the staged walk from
+// W = 7 (measured on B200 at the config-2 shape: W = 7 211 -> 174 us, W = 8 242 -> 192 us; no
+// change up to W = 6). The filter and bias are prescaled by 1/2 when SILU (prescale_filter).
+constexpr int kPairs = 4;
+
+struct Pairs {
+    float2 p[kPairs];
+};
+
+template <typename T>
+__device__ __forceinline__ Pairs to_pairs(const uint4& v) {
+    float f[2 * kPairs];
+    unpack16<T>(v, f);
+    Pairs r;
+#pragma unroll
+    for (int q = 0; q < kPairs; ++q) r.p[q] = make_float2(f[2 * q], f[2 * q + 1]);
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 from_pairs(const Pairs& v) {
+    float f[2 * kPairs];
+#pragma unroll
+    for (int q = 0; q < kPairs; ++q) {
+        f[2 * q] = v.p[q].x;
+        f[2 * q + 1] = v.p[q].y;
+    }
+    return pack16<T>(f);
+}
+
+// The prescaled fp32 filter and bias of load_filter / prescale_filter as channel pairs.
+template <int W>
+__device__ __forceinline__ void filter_pairs(const float (&w)[W][2 * kPairs],
+                                             const float (&b)[2 * kPairs], Pairs (&w2)[W],
+                                             Pairs& b2) {
+#pragma unroll
+    for (int q = 0; q < kPairs; ++q) {
+        b2.p[q] = make_float2(b[2 * q], b[2 * q + 1]);
+#pragma unroll
+        for (int k = 0; k < W; ++k) w2[k].p[q] = make_float2(w[k][2 * q], w[k][2 * q + 1]);
+    }
+}
+
+template <int W, bool SILU>
+__device__ __forceinline__ Pairs conv_step_x2(Pairs (&h)[W - 1], const Pairs& xv,
+                                              const Pairs (&w)[W], const Pairs& b) {
+    constexpr int K = W - 1;
+    Pairs o;
+#pragma unroll
+    for (int q = 0; q < kPairs; ++q) {
+        float2 acc = b.p[q];
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = __ffma2_rn(h[k].p[q], w[k].p[q], acc);
+        acc = __ffma2_rn(xv.p[q], w[K].p[q], acc);
+        if (SILU) acc = __ffma2_rn(acc, make_float2(tanh_approx(acc.x), tanh_approx(acc.y)), acc);
+        o.p[q] = acc;
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k) h[k] = h[k + 1];
+    h[K - 1] = xv;
+    return o;
+}
+
 // Stage of a short strip in shared memory, for the staged kernels: a thread's 16-byte column of
 // the K rows before t0 and of the strip's rows t0.. t0+n-1 (n == S when FULL) lies at
 // col[r * NT], halo rows first. The halo rows at t >= 0 and the strip's first half are one

@@ -138,3 +138,40 @@ def test_channel_first_prefill_16_byte_aligned_stream(dtype):
     ys = causal_conv1d_fn(xs, w, None, "silu")
     torch.cuda.synchronize()
     assert torch.equal(y, ys)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("W", [3, 4, 6, 8])
+def test_strided_weights_take_the_register_walk(W):
+    """The staged kernels read the contiguous (dim, W) weights and a contiguous bias; strided views
+    of them go to the register walks, which must give the same bits (prefill, prefill with
+    states, token-major varlen)."""
+    from causal_conv1d_cute import causal_conv1d_fwd_states
+
+    B, L, D, K = 2, 300, 1024, W - 1
+    g = torch.Generator(device="cuda").manual_seed(W)
+    x = torch.randn(B, L, D, device="cuda", generator=g).to(torch.bfloat16)
+    w = (torch.rand(D, W, device="cuda", generator=g) - 0.5).to(torch.bfloat16)
+    b = (torch.randn(D, device="cuda", generator=g) * 0.1).to(torch.bfloat16)
+    wide_w = torch.zeros(D, W + 1, device="cuda", dtype=torch.bfloat16)
+    wide_w[:, :W] = w
+    wide_b = torch.zeros(D, 2, device="cuda", dtype=torch.bfloat16)
+    wide_b[:, 0] = b
+    ws, bs = wide_w[:, :W], wide_b[:, 0]
+    assert not ws.is_contiguous() and not bs.is_contiguous()
+    xv = x.transpose(1, 2)
+    assert torch.equal(causal_conv1d_fn(xv, w, b, "silu"), causal_conv1d_fn(xv, ws, bs, "silu"))
+    init = torch.randn(B, K, D, device="cuda", generator=g).to(torch.bfloat16).transpose(1, 2)
+    y1, f1 = causal_conv1d_fwd_states(xv, w, b, None, init, True, None, "silu")
+    y2, f2 = causal_conv1d_fwd_states(xv, ws, bs, None, init, True, None, "silu")
+    assert torch.equal(y1, y2) and torch.equal(f1, f2)
+    qsl = torch.tensor([0, 5, 133, 290, 600], device="cuda", dtype=torch.int32)
+    xt = x.reshape(B * L, D)
+    st0 = torch.randn(6, D, K, device="cuda", generator=g).to(torch.bfloat16)
+    cidx = torch.tensor([4, 0, 2, 5], device="cuda", dtype=torch.int32)
+    hinit = torch.tensor([True, False, True, True], device="cuda")
+    s1, s2 = st0.clone(), st0.clone()
+    v1 = causal_conv1d_varlen_fn(xt.t(), w, b, qsl, cidx, hinit, s1, "silu")
+    v2 = causal_conv1d_varlen_fn(xt.t(), ws, bs, qsl, cidx, hinit, s2, "silu")
+    torch.cuda.synchronize()
+    assert torch.equal(v1, v2) and torch.equal(s1, s2)
