@@ -196,6 +196,18 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialisation may
+// start once every CTA of the kernel before it in the stream has called allow_dependent_launch()
+// (or exited); grid_dependency_wait() then blocks until that kernel has completed and its memory
+// writes are visible. Both are hardware dependency controls, not spin loops, and are no-ops for a
+// kernel launched the ordinary way.
+__device__ __forceinline__ void allow_dependent_launch() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // A thread's channel vector of NB bytes (16: uint4, 8: uint2) for the kernels that can run with
 // half-width vectors (fewer registers per thread when the filter is wide).
 template <int NB>

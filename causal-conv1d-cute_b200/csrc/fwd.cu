@@ -245,6 +245,9 @@ __global__ void __launch_bounds__(kCfThreads)
     constexpr int WSPAN = 32 * EPT;  // elements per warp iteration
     const unsigned FULL = 0xffffffffu;
     const int lane = threadIdx.x & 31;
+    // A programmatic dependent (the channel-first varlen boundary pass) may start as this grid's
+    // CTAs retire; it waits for this grid before writing anything this grid writes.
+    allow_dependent_launch();
     const int64_t gw = ((int64_t)blockIdx.x * kCfThreads + threadIdx.x) >> 5;
     const int64_t base = gw * (int64_t)iters * WSPAN;
     if (base >= total) return;  // warp-uniform

@@ -293,6 +293,7 @@ __device__ __forceinline__ void owner_channel(const VarArgs& a, int64_t c, int64
     float h[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) h[k] = to_f32<T>(init[k]);
+    T o[K];
 #pragma unroll
     for (int j = 0; j < K; ++j) {
         const float xv = to_f32<T>(head[j]);
@@ -300,7 +301,7 @@ __device__ __forceinline__ void owner_channel(const VarArgs& a, int64_t c, int64
 #pragma unroll
         for (int k = 0; k < K; ++k) acc = fmaf(h[k], wf[k], acc);
         acc = fmaf(xv, wf[K], acc);
-        if (j < n) orow[bos + j] = from_f32<T>(activate<T>(acc, use_silu));
+        o[j] = from_f32<T>(activate<T>(acc, use_silu));
 #pragma unroll
         for (int k = 0; k + 1 < K; ++k) h[k] = h[k + 1];
         h[K - 1] = xv;
@@ -319,10 +320,19 @@ __device__ __forceinline__ void owner_channel(const VarArgs& a, int64_t c, int64
             sp[k * a.s_sk] = v;
         }
     }
+    // The head outputs replace the bulk pass's values, so they wait for it; everything above
+    // (reads of x and of the cache, the final state) is independent of the bulk pass.
+    grid_dependency_wait();
+#pragma unroll
+    for (int j = 0; j < K; ++j)
+        if (j < n) orow[bos + j] = o[j];
 }
 
 // Second launch of the channel-first path: one thread per (channel, sequence) does the owner work
 // (initial state in, final state out, first W-1 outputs, which replace the bulk pass's values).
+// It is launched as a programmatic dependent of the bulk pass: its CTAs start as the bulk pass's
+// CTAs retire, issue their loads and write the final states at once, and wait for the bulk pass
+// only before writing the head outputs (owner_channel).
 template <typename T, int W>
 __global__ void __launch_bounds__(kBoundaryThreads) varlen_boundary_kernel(const VarArgs a) {
     const int64_t c = (int64_t)blockIdx.x * kBoundaryThreads + threadIdx.x;
@@ -529,9 +539,17 @@ cudaError_t run_varlen(const VarArgs& a, int dtype, cudaStream_t stream) {
         f.silu = a.silu;
         cudaError_t err = launch_fwd(f, W, dtype, stream);
         if (err != cudaSuccess) return err;
-        dim3 grid((unsigned)ceil_div(a.D, kBoundaryThreads), (unsigned)a.nseq);
-        varlen_boundary_kernel<T, W><<<grid, kBoundaryThreads, 0, stream>>>(a);
-        return cudaGetLastError();
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)ceil_div(a.D, kBoundaryThreads), (unsigned)a.nseq);
+        cfg.blockDim = dim3(kBoundaryThreads);
+        cfg.dynamicSmemBytes = 0;
+        cfg.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, varlen_boundary_kernel<T, W>, a);
     }
     const int strip = 64;
     const int64_t n = ceil_div(a.T, strip) * a.D;
