@@ -11,7 +11,7 @@
 // (zeros in place of init without initial states), copied bit for bit from the inputs.
 //
 // Kernels:
-//   fwd_states_staged_kernel  channel-last x / out, 16-bit types, no sequence ids: the
+//   fwd_states_staged_kernel  channel-last x / out, 16-bit types, contiguous weights: the
 //                           staged strips of the plain prefill (one per CTA, landed in
 //                           shared memory), initial states in the halo of a row's first strip.
 //   fwd_states_vec_kernel   channel-last x / out otherwise (16-byte channel vectors, the walk and
@@ -136,10 +136,10 @@ __global__ void __launch_bounds__(kStThreads)
 // Staged form for 16-bit types (the launch table of the plain prefill, fwd.cu): one
 // CTA per strip of S tokens of one batch row and NT channel vectors, the strip landed in shared
 // memory by cp.async (stage_strip). History before token 0 is the initial states (zeros without
-// them), written into the stage's halo rows; the strip that ends a row writes that row's final
-// states. Calls with sequence ids keep the register walk (see the launch table). FULL: a whole
-// strip of S rows (no per-row guard, see the plain staged kernel).
-template <typename T, int W, int S, int NT, bool SILU, bool FULL>
+// them), written into the stage's halo rows; with sequence ids (SEQ) a tap counts only when its id
+// equals the token's; the strip that ends a row writes that row's final states. FULL: a whole strip
+// of S rows (no per-row guard, see the plain staged kernel).
+template <typename T, int W, int S, int NT, bool SILU, bool SEQ, bool FULL>
 __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, int64_t b,
                                              int64_t t0, int64_t n, int64_t c0) {
     constexpr int V = Vec<T>::V;
@@ -149,6 +149,10 @@ __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, 
     const T* xb = (const T*)f.x + b * f.x_sb + c0;
     stage_strip<T, K, S, NT, FULL>(col, xb, f.x_sl, t0, n);
     const T* init = (const T*)a.init;
+    // Sequence ids of the halo and the strip's rows (rows before token 0 carry none: their values
+    // are zeros or initial states, which sequence ids exclude).
+    int32_t qh[K], q[S];
+    const int32_t* qb = SEQ ? a.seq + b * a.q_sb : nullptr;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
         const int64_t t = t0 - K + k;
@@ -160,6 +164,25 @@ __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, 
                     set_lane<T>(v, e, init[b * a.i_sb + (c0 + e) * a.i_sd + (K + t) * a.i_sk]);
             }
             col[k * NT] = v;
+        }
+        if (SEQ) qh[k] = t >= 0 ? __ldg(qb + t * a.q_sl) : INT32_MIN;
+    }
+    if (SEQ) {
+        const int32_t* qr = qb + t0 * a.q_sl;
+        if (FULL && a.q_sl == 1 && aligned16(qr)) {
+            // Contiguous, aligned ids: four to a 16-byte load.
+#pragma unroll
+            for (int g = 0; g < S / 4; ++g) {
+                const int4 v = __ldg(reinterpret_cast<const int4*>(qr) + g);
+                q[4 * g] = v.x;
+                q[4 * g + 1] = v.y;
+                q[4 * g + 2] = v.z;
+                q[4 * g + 3] = v.w;
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < S; ++r)
+                if (FULL || r < n) q[r] = __ldg(qr + r * a.q_sl);
         }
     }
     Pairs w2[W], b2;
@@ -173,7 +196,9 @@ __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, 
     T* ob = (T*)f.out + b * f.o_sb + c0;
     Pairs h[K];
     auto row = [&](int r) {
-        const Pairs o = conv_step_x2<W, SILU>(h, to_pairs<T>(col[(K + r) * NT]), w2, b2);
+        const Pairs xv = to_pairs<T>(col[(K + r) * NT]);
+        const Pairs o = SEQ ? conv_step_x2_seq<W, SILU>(h, qh, xv, q[r], w2, b2)
+                            : conv_step_x2<W, SILU>(h, xv, w2, b2);
         st16_stream(ob + (t0 + r) * f.o_sl, from_pairs<T>(o));
     };
     cp_async_wait<1>();
@@ -187,14 +212,16 @@ __device__ __forceinline__ void states_strip(const FwdStateArgs& a, uint4* col, 
         for (int r = HALF; r < S; ++r) row(r);
     } else {
         cp_async_wait<0>();
-        for (int r = 0; r < n; ++r) row(r);
+#pragma unroll
+        for (int r = 0; r < S; ++r)
+            if (r < n) row(r);
     }
     if (a.fin != nullptr && t0 + n == f.L) states_final<T, W>(a, b, c0, V);
 }
 
 // Strips strip0 .. strip0 + nstrips - 1 of every batch row: whole strips (FULL) in one launch, each
 // row's last partial strip in a second one, as the plain staged prefill (fwd.cu).
-template <typename T, int W, int S, int NT, bool SILU, bool FULL>
+template <typename T, int W, int S, int NT, bool SILU, bool SEQ, bool FULL>
 __global__ void __launch_bounds__(NT)
     fwd_states_staged_kernel(const FwdStateArgs a, int64_t nstrips, int64_t gx, int64_t strip0) {
     constexpr int V = Vec<T>::V;
@@ -206,19 +233,19 @@ __global__ void __launch_bounds__(NT)
     const int64_t b = su / nstrips;
     const int64_t t0 = (strip0 + su - b * nstrips) * S;
     const int64_t n = FULL ? S : a.f.L - t0;
-    states_strip<T, W, S, NT, SILU, FULL>(a, stage + threadIdx.x, b, t0, n, j * V);
+    states_strip<T, W, S, NT, SILU, SEQ, FULL>(a, stage + threadIdx.x, b, t0, n, j * V);
 }
 
-template <typename T, int W, int S, int NT, bool SILU>
+template <typename T, int W, int S, int NT, bool SILU, bool SEQ>
 cudaError_t launch_states_staged(const FwdStateArgs& a, int64_t gx, cudaStream_t stream) {
     const size_t smem = (size_t)(S + W - 1) * NT * 16;
     const int64_t full = a.f.L / S;
     if (full > 0) {
-        fwd_states_staged_kernel<T, W, S, NT, SILU, true>
+        fwd_states_staged_kernel<T, W, S, NT, SILU, SEQ, true>
             <<<(unsigned)(gx * a.f.B * full), NT, smem, stream>>>(a, full, gx, 0);
     }
     if (a.f.L % S != 0) {
-        fwd_states_staged_kernel<T, W, S, NT, SILU, false>
+        fwd_states_staged_kernel<T, W, S, NT, SILU, SEQ, false>
             <<<(unsigned)(gx * a.f.B), NT, smem, stream>>>(a, 1, gx, full);
     }
     return cudaGetLastError();
@@ -306,16 +333,18 @@ cudaError_t run_fwd_states(const FwdStateArgs& a, cudaStream_t stream) {
         // channel-last prefill (channel pairs, compile-time SiLU).
         // Measured on B200 at the config-2 shape (bf16, W = 4), staged vs the balanced register
         // walk below: initial + final states 163.3 vs 182.9 us (172.5 with scalar FMAs and a
-        // run-time SiLU); with sequence ids a staged form with scalar FMAs took 183.4 vs 181.3 us
-        // (the per-row ids and masked taps cost more than staging saves), so calls with sequence
-        // ids keep the register walk.
+        // run-time SiLU); with sequence ids 170.4 vs 181.4 us (183.4 with scalar FMAs, 184.3 with
+        // the 16 ids of a strip loaded one by one instead of four to a 16-byte load).
         constexpr int S = W == 8 ? 32 : 16, NT = 64;
         const int64_t gx = ceil_div(f.D / V, (int64_t)NT);
         const int64_t blocks = gx * f.B * ceil_div(f.L, (int64_t)S);
-        if (cl && f.L > 0 && a.seq == nullptr && wvec && (f.bias == nullptr || bvec) &&
-            blocks <= 0x7fffffffLL)
-            return f.silu ? launch_states_staged<T, W, S, NT, true>(a, gx, stream)
-                          : launch_states_staged<T, W, S, NT, false>(a, gx, stream);
+        if (cl && f.L > 0 && wvec && (f.bias == nullptr || bvec) && blocks <= 0x7fffffffLL) {
+            if (a.seq != nullptr)
+                return f.silu ? launch_states_staged<T, W, S, NT, true, true>(a, gx, stream)
+                              : launch_states_staged<T, W, S, NT, false, true>(a, gx, stream);
+            return f.silu ? launch_states_staged<T, W, S, NT, true, false>(a, gx, stream)
+                          : launch_states_staged<T, W, S, NT, false, false>(a, gx, stream);
+        }
     }
     if (cl) {
         // Launch table as for the plain channel-last prefill (fwd.cu): many ~128-row shares,

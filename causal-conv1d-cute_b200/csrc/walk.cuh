@@ -265,6 +265,34 @@ __device__ __forceinline__ Pairs conv_step_x2(Pairs (&h)[W - 1], const Pairs& xv
     return o;
 }
 
+// conv_step_x2 with per-token sequence ids: a history tap counts only when its id equals the
+// token's id q (the term is skipped, as in conv_step_seq); the window ids qh shift with the values.
+template <int W, bool SILU>
+__device__ __forceinline__ Pairs conv_step_x2_seq(Pairs (&h)[W - 1], int32_t (&qh)[W - 1],
+                                                  const Pairs& xv, int32_t q, const Pairs (&w)[W],
+                                                  const Pairs& b) {
+    constexpr int K = W - 1;
+    Pairs o;
+#pragma unroll
+    for (int p = 0; p < kPairs; ++p) {
+        float2 acc = b.p[p];
+#pragma unroll
+        for (int k = 0; k < K; ++k)
+            if (qh[k] == q) acc = __ffma2_rn(h[k].p[p], w[k].p[p], acc);
+        acc = __ffma2_rn(xv.p[p], w[K].p[p], acc);
+        if (SILU) acc = __ffma2_rn(acc, make_float2(tanh_approx(acc.x), tanh_approx(acc.y)), acc);
+        o.p[p] = acc;
+    }
+#pragma unroll
+    for (int k = 0; k + 1 < K; ++k) {
+        h[k] = h[k + 1];
+        qh[k] = qh[k + 1];
+    }
+    h[K - 1] = xv;
+    qh[K - 1] = q;
+    return o;
+}
+
 // Stage of a short strip in shared memory, for the staged kernels: a thread's 16-byte column of
 // the K rows before t0 and of the strip's rows t0.. t0+n-1 (n == S when FULL) lies at
 // col[r * NT], halo rows first. The halo rows at t >= 0 and the strip's first half are one

@@ -74,16 +74,20 @@ def test_empty_sequence_returns_the_initial_state_tail():
 @pytest.mark.parametrize("layout", ["btd", "bdl"])
 @pytest.mark.parametrize("W", [2, 4, 8])
 def test_sequence_ids(W, layout):
-    B, D, L = 2, 256, 300
-    x, w, b, _ = _inputs(B, D, L, W, torch.bfloat16, layout, 40 + W)
-    rng = np.random.default_rng(W)
-    cuts = [np.sort(rng.choice(np.arange(1, L), 6, replace=False)) for _ in range(B)]
-    seq = np.stack([np.searchsorted(c, np.arange(L), side="right") for c in cuts]).astype(np.int32)
-    seq[1, 200:205] = 0  # an id that recurs after other ids
-    out = causal_conv1d_fwd_states(x, w, b, torch.from_numpy(seq).cuda(), None, False, None, "silu")
-    torch.cuda.synchronize()
-    r_out, _ = oracle.fwd_states(to_np(x), to_np(w), to_np(b), seq, None, True, "bf16")
-    assert_close(out, r_out, torch.bfloat16)
+    # L = 301: the second row's ids start 4 bytes past a 16-byte line, so the staged kernel loads
+    # them one by one there and four to a 16-byte load in the first row.
+    for L in (300, 301):
+        B, D = 2, 256
+        x, w, b, _ = _inputs(B, D, L, W, torch.bfloat16, layout, 40 + W)
+        rng = np.random.default_rng(W)
+        cuts = [np.sort(rng.choice(np.arange(1, L), 6, replace=False)) for _ in range(B)]
+        seq = np.stack([np.searchsorted(c, np.arange(L), side="right") for c in cuts]).astype(np.int32)
+        seq[1, 200:205] = 0  # an id that recurs after other ids
+        out = causal_conv1d_fwd_states(x, w, b, torch.from_numpy(seq).cuda(), None, False, None,
+                                       "silu")
+        torch.cuda.synchronize()
+        r_out, _ = oracle.fwd_states(to_np(x), to_np(w), to_np(b), seq, None, True, "bf16")
+        assert_close(out, r_out, torch.bfloat16)
 
 
 @pytest.mark.gpu
