@@ -1000,6 +1000,11 @@ def _profile_other(dev, g, width, case):
         init = torch.randn(2, 3, D, device=dev, generator=g).to(BF).transpose(1, 2)
         fin = torch.empty_like(init)
         return lambda: C.causal_conv1d_fwd_states(x, w, b, None, init, True, fin, "silu")
+    if case == "states_seq":  # config 2 with batch 2, two sequence ids per row
+        x = torch.randn(2, L, D, device=dev, generator=g).to(BF).transpose(1, 2)
+        seq = torch.zeros(2, L, device=dev, dtype=torch.int32)
+        seq[:, L // 2:] = 1
+        return lambda: C.causal_conv1d_fwd_states(x, w, b, seq, None, False, None, "silu")
     # copy: the headline's bytes of batch 2 (128 MiB in, 128 MiB out)
     import causal_conv1d_cute.testing as T
 
@@ -1021,6 +1026,7 @@ PROFILE_CASES = {
     "spec": lambda d, g, w: _profile_other(d, g, w, "spec"),
     "unpack": lambda d, g, w: _profile_other(d, g, w, "unpack"),
     "states": lambda d, g, w: _profile_other(d, g, w, "states"),
+    "states_seq": lambda d, g, w: _profile_other(d, g, w, "states_seq"),
     "fwd_generic": lambda d, g, w: _profile_other(d, g, w, "fwd_generic"),
     "update_generic": lambda d, g, w: _profile_other(d, g, w, "update_generic"),
     "copy": lambda d, g, w: _profile_other(d, g, w, "copy"),
