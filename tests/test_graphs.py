@@ -43,6 +43,33 @@ def test_prefill_and_varlen_in_a_graph():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("W", [4, 8])
+def test_channel_first_varlen_in_a_graph(W):
+    """Channel-first varlen is two launches, the second a programmatic dependent of the first; the
+    captured pair, replayed twice, must equal two eager calls (outputs and cache)."""
+    torch.manual_seed(W)
+    D, T = 512, 1000
+    xv = torch.randn(D, T, device="cuda", dtype=torch.bfloat16)  # contiguous (dim, tokens)
+    w = torch.randn(D, W, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(D, device="cuda", dtype=torch.bfloat16)
+    qsl = torch.tensor([0, 3, 150, 151, 600, 1000], device="cuda", dtype=torch.int32)
+    cidx = torch.tensor([5, 0, 2, 6, 1], device="cuda", dtype=torch.int32)
+    h = torch.tensor([True, False, True, True, False], device="cuda")
+    st0 = torch.randn(8, D, W - 1, device="cuda", dtype=torch.bfloat16)
+    st = st0.clone()
+    g, y = _capture(lambda: C.causal_conv1d_varlen_fn(xv, w, b, qsl, cidx, h, st, "silu"))
+    st.copy_(st0)
+    g.replay()
+    y1 = y.clone()
+    g.replay()
+    st_e = st0.clone()
+    ye1 = C.causal_conv1d_varlen_fn(xv, w, b, qsl, cidx, h, st_e, "silu")
+    ye2 = C.causal_conv1d_varlen_fn(xv, w, b, qsl, cidx, h, st_e, "silu")
+    torch.cuda.synchronize()
+    assert torch.equal(y1, ye1) and torch.equal(y, ye2) and torch.equal(st, st_e)
+
+
+@pytest.mark.gpu
 def test_decode_paths_in_a_graph():
     torch.manual_seed(1)
     B, D = 16, 1024
