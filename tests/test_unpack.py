@@ -30,6 +30,10 @@ def _inputs(B, D, zdim, heads, W, dtype, gdtype, slots, row_extra=0, seed=0):
         (33, 1024, 512, 16, 4, torch.bfloat16, torch.float32, 16),
         (3, 64, 64, 4, 3, torch.float16, torch.float16, 8),
         (7, 128, 32, 6, 2, torch.float32, torch.bfloat16, 0),
+        # 128 rows and more take the wider CTAs; an odd count leaves a half row pair.
+        (131, 512, 256, 16, 4, torch.bfloat16, torch.bfloat16, 0),
+        (129, 256, 64, 8, 8, torch.float16, torch.float32, 8),
+        (130, 96, 32, 40, 6, torch.bfloat16, torch.float32, 0),
     ],
 )
 def test_unpack_against_oracle(B, D, zdim, heads, W, dtype, gdtype, row_extra):
