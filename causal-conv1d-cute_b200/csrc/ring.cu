@@ -32,7 +32,9 @@ __device__ __forceinline__ int ring_pos(int32_t seen, int K) {
 // weights widened at use. Every load of every row is issued before any compute: the slot and
 // count loads first (each heads the only dependent chain, slot -> ring rows), then the filter and
 // the x rows, then the ring rows.
-template <typename T, int W, int NB, int R>
+// MODE 0: weight / bias layout and SiLU read from the arguments. MODE 1-4: contiguous 16-byte
+// aligned weights, and SiLU (2, 4) and a contiguous aligned bias (3, 4) fixed at compile time.
+template <typename T, int W, int NB, int R, int MODE>
 __global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bool wvec, bool bvec) {
     using RV = typename RawVec<NB>::type;
     constexpr int V = NB / (int)sizeof(T);
@@ -48,9 +50,12 @@ __global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bo
         slot[r] = b < a.B ? (a.idx != nullptr ? __ldg(a.idx + b) : (int32_t)b) : a.pad;
         seen[r] = b < a.B ? __ldg(a.seen + b) : 0;
     }
+    constexpr bool kFixed = MODE > 0, kSilu = MODE == 2 || MODE == 4, kBias = MODE >= 3;
+    const bool use_silu = kFixed ? kSilu : a.silu != 0;
     RV wt[W], bt;
-    load_filter_raw<T, W>((const T*)a.w, a.w_sd, a.w_sk, (const T*)a.bias, a.bias_s, c0, wvec,
-                          bvec, wt, bt);
+    load_filter_raw<T, W>((const T*)a.w, a.w_sd, a.w_sk,
+                          kFixed && !kBias ? nullptr : (const T*)a.bias, a.bias_s, c0,
+                          kFixed ? true : wvec, kFixed ? kBias : bvec, wt, bt);
     RV xr[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
@@ -94,7 +99,7 @@ __global__ void __launch_bounds__(kRingThreads) ring_kernel(const RingArgs a, bo
             unpack_raw<T, NB>(xr[r], f);
             unpack_raw<T, NB>(wt[K], wk);
 #pragma unroll
-            for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), a.silu != 0);
+            for (int e = 0; e < V; ++e) acc[e] = activate<T>(fmaf(f[e], wk[e], acc[e]), use_silu);
         }
         T* rb = (T*)a.ring + (int64_t)slot[r] * a.r_slot + c0;
         st_raw<NB>(rb + pos * a.r_sk, xr[r]);
@@ -134,6 +139,19 @@ __global__ void __launch_bounds__(kGenThreads) ring_generic_kernel(const RingArg
     }
 }
 
+template <typename T, int W, int NB, int R>
+cudaError_t launch_ring_mode(int mode, dim3 grid, const RingArgs& a, bool wvec, bool bvec,
+                             cudaStream_t stream) {
+    switch (mode) {
+        case 1: ring_kernel<T, W, NB, R, 1><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec); break;
+        case 2: ring_kernel<T, W, NB, R, 2><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec); break;
+        case 3: ring_kernel<T, W, NB, R, 3><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec); break;
+        case 4: ring_kernel<T, W, NB, R, 4><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec); break;
+        default: ring_kernel<T, W, NB, R, 0><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec); break;
+    }
+    return cudaGetLastError();
+}
+
 template <typename T, int W>
 cudaError_t run_ring(const RingArgs& a, cudaStream_t stream) {
     constexpr int V = Vec<T>::V;
@@ -150,18 +168,22 @@ cudaError_t run_ring(const RingArgs& a, cudaStream_t stream) {
         // graphs, 256 MiB L2 flush before every call; cold / warm us, as (NB bytes, R rows), one
         // run): B = 64: (16, 1) 4.52 / 3.07, (8, 1) 4.10 / 3.01, (8, 2) 3.97 / 2.84,
         // (8, 4) 4.12 / 2.92; B = 256: (16, 1) 8.64 / 6.32, (8, 2) 7.72 / 5.79, (8, 4) 7.18 / 5.00,
-        // (16, 4) 8.34 / 5.22. fp32 keeps one row of 16-byte vectors.
+        // (16, 4) 8.34 / 5.22. fp32 keeps one row of 16-byte vectors. With contiguous weights and
+        // a contiguous or absent bias, the layout switches and SiLU are compile-time (MODE 1-4):
+        // measured inside a torch process (CUDA graphs, the same flush), B = 64 (8, 2) 4.19 / 3.23
+        // -> 3.80 / 3.01 us, B = 256 (8, 4) 7.15-7.33 / 5.56 -> 6.85-6.89 / 5.25.
         if constexpr (sizeof(T) == 2) {
             const int64_t nvec8 = a.D / (8 / (int64_t)sizeof(T));
             const int R = a.B >= 128 ? 4 : 2;
             dim3 grid((unsigned)ceil_div(nvec8, kRingThreads), (unsigned)ceil_div(a.B, (int64_t)R));
-            if (R == 4) ring_kernel<T, W, 8, 4><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
-            else ring_kernel<T, W, 8, 2><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
-            return cudaGetLastError();
+            const int mode = !(wvec && (a.bias == nullptr || bvec)) ? 0
+                             : 1 + (a.silu != 0 ? 1 : 0) + (a.bias != nullptr ? 2 : 0);
+            if (R == 4) return launch_ring_mode<T, W, 8, 4>(mode, grid, a, wvec, bvec, stream);
+            return launch_ring_mode<T, W, 8, 2>(mode, grid, a, wvec, bvec, stream);
         }
         const int64_t nvec = a.D / V;
         dim3 grid((unsigned)ceil_div(nvec, kRingThreads), (unsigned)a.B);
-        ring_kernel<T, W, 16, 1><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
+        ring_kernel<T, W, 16, 1, 0><<<grid, kRingThreads, 0, stream>>>(a, wvec, bvec);
         return cudaGetLastError();
     }
     const int64_t n = a.B * a.D;

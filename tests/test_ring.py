@@ -114,3 +114,31 @@ def test_ring_with_channel_count_not_multiple_of_16():
                                    None, "bf16")
     assert_close(y, r_out, torch.bfloat16)
     assert_bits(from_ring(ring, seen + 1), r_st)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [5, 130])
+@pytest.mark.parametrize("form", ["plain", "silu", "bias", "silu+bias", "strided"])
+def test_ring_decode_flag_forms(B, form):
+    """Each compile-time form of the 16-bit ring kernel (SiLU and a contiguous bias on or off) and
+    the run-time form that strided weights and a strided bias take, against the oracle."""
+    torch.manual_seed(B)
+    D, W = 1024, 4
+    dtype = torch.bfloat16
+    act = "silu" if "silu" in form or form == "strided" else None
+    if form == "strided":
+        w = torch.randn(D, W + 3, device="cuda", dtype=dtype)[:, 1:W + 1]
+        b = torch.randn(D, 2, device="cuda", dtype=dtype)[:, 1]
+    else:
+        w = torch.randn(D, W, device="cuda", dtype=dtype)
+        b = torch.randn(D, device="cuda", dtype=dtype) if "bias" in form else None
+    ordered = torch.randn(B, D, W - 1, device="cuda", dtype=dtype)
+    seen = torch.randint(0, 50, (B,), device="cuda", dtype=torch.int32)
+    ring = to_ring(ordered, seen).contiguous()
+    x = torch.randn(B, D, device="cuda", dtype=dtype)
+    ring_before = to_np(ring)
+    y = causal_conv1d_update_ring(x, ring, w, b, act, seen)
+    r_out, r_ring = oracle.update_ring(to_np(x), ring_before, to_np(w), to_np(b), act is not None,
+                                       to_np(seen), None, PAD, TAG[dtype])
+    assert_close(y, r_out, dtype)
+    assert_bits(ring, r_ring)
